@@ -1,0 +1,164 @@
+/*
+ * vlcache_b200 — C ABI of the B200-native (sm_100a) warm-prefill attention path
+ * for Qwen2.5-VL in VLCache / nano-vllm.
+ *
+ * Every entry point takes plain device pointers, element strides, int32
+ * metadata and a CUDA stream (passed as `void*`, NULL = legacy default stream),
+ * and returns an int status (VLC_OK = 0).  No entry point allocates device
+ * memory: callers own the KV cache, metadata, outputs and workspaces.
+ * Argument errors are reported before any launch; data-dependent errors found
+ * on the device (e.g. an out-of-range slot) are recorded in a device error
+ * word that vlc_get_device_error() reads.
+ *
+ * Layout conventions (all bf16 unless stated):
+ *   q        [num_tokens, num_heads, head_dim]      token stride given, head stride = head_dim
+ *   key/value[num_tokens, num_kv_heads, head_dim]   token stride given (views of the QKV split)
+ *   k_cache/v_cache per layer [num_slots, num_kv_heads, head_dim] contiguous,
+ *            num_slots = num_blocks * block_size  (nano-vllm: [num_blocks, 256, Hk, D])
+ *   block_tables [num_seqs, block_table_stride] int32, padded with -1
+ *   slot_mapping [num_tokens] int32, -1 = skip
+ */
+#ifndef VLCACHE_B200_H
+#define VLCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host side) ---- */
+#define VLC_OK 0
+#define VLC_ERR_NULL 1        /* required pointer is NULL */
+#define VLC_ERR_SHAPE 2       /* unsupported or inconsistent sizes */
+#define VLC_ERR_STRIDE 3      /* stride/contiguity requirement violated */
+#define VLC_ERR_ALIGN 4       /* pointer/stride not 16-byte aligned */
+#define VLC_ERR_UNSUPPORTED 5 /* e.g. head_dim != 128 */
+#define VLC_ERR_WORKSPACE 6   /* workspace missing or too small */
+#define VLC_ERR_CUDA 7        /* a CUDA runtime/driver call failed */
+#define VLC_ERR_PLAN 8        /* plan buffer malformed or too small */
+#define VLC_ERR_METADATA 9    /* cu_seqlens / lengths inconsistent */
+
+/* ---- device error codes (recorded by kernels, read by vlc_get_device_error) ---- */
+#define VLC_DEV_ERR_SLOT_RANGE 101   /* slot >= num_slots or < -1 */
+#define VLC_DEV_ERR_BLOCK_RANGE 102  /* block table entry out of range where a key is needed */
+#define VLC_DEV_ERR_TIMEOUT 110      /* an mbarrier wait hit its bound (base; +role id) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int vlc_version(void);
+
+/* Human-readable text for a status code. */
+const char* vlc_status_string(int status);
+
+/* Synchronises the current device and returns its device error word (0 = none).
+ * reset != 0 clears the word afterwards. */
+int vlc_get_device_error(int reset);
+
+/* Number of SMs of the current device (used by the planners). */
+int vlc_num_sms(void);
+
+/* --------------------------------------------------------------------------
+ * KV scatter.
+ * Replaces nanovllm/layers/attention.py:10-40 (store_kvcache_kernel + store_kvcache):
+ *   k_cache.view(-1, D)[slot_mapping[i]] = key[i];  v_cache likewise;  slot -1 skipped.
+ * key/value rows are row_elems = num_kv_heads*head_dim contiguous bf16 elements;
+ * key_stride/value_stride are token strides in elements.  Bit-exact copy.
+ * ------------------------------------------------------------------------ */
+int vlc_store_kvcache(const void* key, int64_t key_stride, const void* value, int64_t value_stride,
+                      void* k_cache, void* v_cache, const int32_t* slot_mapping, int num_tokens,
+                      int row_elems, int64_t num_slots, void* stream);
+
+/* --------------------------------------------------------------------------
+ * M-RoPE position shift of reused vision K (new capability; replaces the
+ * verbatim row copy of nanovllm/engine/model_runner.py:170-180 copy_image_kv,
+ * driven by nanovllm/engine/llm_engine.py:58-89).
+ * For each of num_layers layers (layer l at k_cache + l*layer_stride elements)
+ * and each row i: K row at src_slots[i] is rotated by the per-section position
+ * delta (delta_thw[0..2] for the t/h/w sections of mrope_section[0..2] pairs)
+ * and written to dst_slots[i] (dst_slots == NULL: in place).  When v_cache is
+ * non-NULL and dst_slots is non-NULL, the V row is copied verbatim too.
+ * RoPE convention: rotate-half pairs (j, j + head_dim/2), inv_freq[j] =
+ * theta^(-2j/head_dim) (HF transformers modeling_qwen2_5_vl.py:627-665).
+ * Math in fp32 with a host-built cos/sin table; bf16 storage.
+ * src/dst rows must be disjoint sets (or dst == src in place).
+ * ------------------------------------------------------------------------ */
+int vlc_mrope_shift(void* k_cache, void* v_cache, int64_t layer_stride, int num_layers,
+                    int64_t num_slots, int num_kv_heads, int head_dim, const int32_t* src_slots,
+                    const int32_t* dst_slots, int num_rows, const int32_t* delta_thw,
+                    const int32_t* mrope_section, float rope_theta, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Warm-prefill attention plan (host-only, no CUDA calls).
+ * Replaces the work decomposition flash-attn derives inside
+ * flash_attn_varlen_func (called at nanovllm/layers/attention.py:64-70).
+ * Inputs are HOST copies of cu_seqlens_q / cu_seqlens_k ([num_seqs+1]).
+ * Query row i of sequence b has logical position
+ *   k_len_b - q_len_b + i   (causal, bottom-right aligned, as flash-attn).
+ * Writes an int32 plan into plan_out (capacity plan_capacity ints) and returns
+ * VLC_OK; *plan_len receives the number of ints used.  num_sms = 0 queries the
+ * current device (falls back to 148 without a device).
+ * ------------------------------------------------------------------------ */
+int vlc_prefill_plan(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs,
+                     int num_heads, int num_kv_heads, int head_dim, int num_sms,
+                     int32_t* plan_out, int64_t plan_capacity, int64_t* plan_len);
+
+/* Upper bound (ints) of the plan for these sequences. */
+int64_t vlc_prefill_plan_capacity(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                                  int num_seqs, int num_heads, int num_kv_heads, int num_sms);
+
+/* Workspace bytes vlc_prefill_attn needs for a given (host) plan. */
+int64_t vlc_prefill_workspace_size(const int32_t* plan_host);
+
+/* --------------------------------------------------------------------------
+ * Sparse-query paged prefill attention (tcgen05 / TMEM / TMA, sm_100a).
+ * Replaces flash_attn_varlen_func(q, k, v, cu_seqlens_q, cu_seqlens_k,
+ * max_seqlen_q, max_seqlen_k, softmax_scale, causal=True, block_table=...)
+ * at nanovllm/layers/attention.py:64-70, both of its branches:
+ *   paged      (block_tables != NULL): k/v are one layer's caches, key j of
+ *              sequence b lives at row block_tables[b][j / block_size] *
+ *              block_size + j % block_size (block_size a multiple of 128);
+ *   contiguous (block_tables == NULL): key j of sequence b is row
+ *              cu_seqlens_k[b] + j of k/v (the in-flight K/V of a cold prefill).
+ *   o[i, h, :] = softmax(scale * q[i,h,:] . K[j, h/G, :]^T, j <= pos(i)) V
+ * with GQA group G = num_heads / num_kv_heads.  k_row_stride / v_row_stride
+ * are the element strides between consecutive key rows (num_kv_heads*head_dim
+ * for a cache); num_kv_rows is the number of rows addressable through k/v.
+ * plan_dev is the plan from vlc_prefill_plan copied to device memory;
+ * plan_host is the same plan on the host (only its header is read).
+ * out: [total_q, num_heads, head_dim] bf16 with token stride out_token_stride.
+ * head_dim must be 128.
+ * ------------------------------------------------------------------------ */
+int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num_heads,
+                     const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
+                     int64_t num_kv_rows, int num_kv_heads, int head_dim,
+                     const int32_t* block_tables, int block_table_stride, int block_size,
+                     const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
+                     void* out, int64_t out_token_stride, void* workspace,
+                     int64_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Split-K paged flash-decode.
+ * Replaces flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+ * cache_seqlens=context_lens, block_table=block_tables, softmax_scale, causal=True)
+ * at nanovllm/layers/attention.py:71-74 (one query token per sequence).
+ * q: [num_seqs, num_heads, head_dim] (token stride q_seq_stride); out likewise.
+ * context_lens [num_seqs] int32 on device; max_context_len is a host-side upper
+ * bound used only to size the grid (graph-capture safe: no host reads).
+ * ------------------------------------------------------------------------ */
+int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs, int num_heads,
+                    const void* k_cache, const void* v_cache, int64_t num_slots, int num_kv_heads,
+                    int head_dim, const int32_t* block_tables, int block_table_stride,
+                    int block_size, const int32_t* context_lens, int max_context_len,
+                    float softmax_scale, void* out, int64_t out_seq_stride, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes vlc_decode_attn needs. */
+int64_t vlc_decode_workspace_size(int num_seqs, int num_heads, int num_kv_heads,
+                                  int max_context_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VLCACHE_B200_H */

@@ -1,0 +1,148 @@
+"""Host logic of the product (no GPU): metadata builder, image-reuse slots, the
+attention planner (through the C ABI), and the loud failure of the CUDA-only ops."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from vlcache_b200.engine import kv_cache as kvc
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def _reqs(g):
+    out = []
+    for i, (n, s, e, R, partial) in enumerate(g["requests"]):
+        bt = [int(x) for x in g["request_block_tables"][i] if x >= 0]
+        out.append(kvc.WarmRequest(int(n), bt, int(s) if s >= 0 else None, int(e) if e >= 0 else None, int(R),
+                                   bool(partial)))
+    return out
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "mixed"])
+def test_builder_bit_exact_vs_reference(name):
+    g = dict(np.load(GOLD / f"metadata_{name}.npz"))
+    b = kvc.WarmPrefillBuilder(16, 2).build(_reqs(g))
+    assert np.array_equal(b.cu_seqlens_q, g["cu_seqlens_q"])
+    assert np.array_equal(b.cu_seqlens_k, g["cu_seqlens_k"])
+    assert np.array_equal(b.slot_mapping, g["slot_mapping"])
+    assert np.array_equal(b.positions, g["positions"])
+    assert np.array_equal(b.block_tables, g["block_tables"])
+    assert b.max_seqlen_q == int(g["max_seqlen_q"]) and b.max_seqlen_k == int(g["max_seqlen_k"])
+    assert list(b.logit_indices) == list(g["logit_indices"])
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "mixed"])
+def test_image_reuse_slots_vs_reference(name):
+    g = dict(np.load(GOLD / f"metadata_{name}.npz"))
+    src, dst = [], []
+    for r in _reqs(g):
+        if r.partial:
+            s, d = kvc.image_reuse_slots(r.img_start, r.img_end, r.num_recompute, r.block_table,
+                                         int(g["cold_img_start"]), g["cold_block_table"])
+            src.append(s)
+            dst.append(d)
+    assert np.array_equal(np.concatenate(src), g["old_slots"])
+    assert np.array_equal(np.concatenate(dst), g["new_slots"])
+    # new pages are freshly allocated: source and destination never overlap
+    assert not set(np.concatenate(src).tolist()) & set(np.concatenate(dst).tolist())
+
+
+def test_recompute_count():
+    assert kvc.recompute_count(0.1, 10549) == 1055
+    assert kvc.recompute_count(0.05, 2691) == 135
+
+
+# ---------------------------------------------------------------- planner (C ABI, host only)
+def _decode_plan(plan):
+    from vlcache_b200 import ops  # noqa: F401  (loads the library)
+    h = plan.host
+    grid, nu, nparts, nm = int(h[2]), int(h[3]), int(h[4]), int(h[5])
+    cta = h[int(h[12]):int(h[12]) + grid + 1]
+    units = h[int(h[13]):int(h[13]) + nu * 12].reshape(nu, 12)
+    merges = h[int(h[14]):int(h[14]) + nm * 8].reshape(nm, 8)
+    return grid, cta, units, merges, nparts
+
+
+def _coverage(cu_q, cu_k, H, Hk, num_sms):
+    from vlcache_b200 import ops
+    plan = ops.build_prefill_plan(cu_q, cu_k, H, Hk, num_sms=num_sms)
+    grid, cta, units, merges, nparts = _decode_plan(plan)
+    G = H // Hk
+    T = 128 // G
+    assert int(plan.host[6]) == T * G and int(plan.host[7]) == T
+    assert cta[0] == 0 and cta[-1] == len(units) and np.all(np.diff(cta) >= 0)
+    assert grid <= num_sms
+    # every (query token, kv head, key block) visible under the causal mask is covered exactly once
+    need = {}
+    for b in range(len(cu_q) - 1):
+        ql, kl = cu_q[b + 1] - cu_q[b], cu_k[b + 1] - cu_k[b]
+        for g in range(Hk):
+            for t in range(ql):
+                pos = kl - ql + t
+                for kb in range(pos // 128 + 1):
+                    need[(cu_q[b] + t, g, kb)] = 0
+    parts_seen = set()
+    for u in units:
+        seq, g, qb, qc, kp0, kb0, kb1, kvl, part = [int(x) for x in u[:9]]
+        assert 1 <= qc <= T and kb0 < kb1
+        assert kvl == cu_k[seq + 1] - cu_k[seq] and int(u[10]) == cu_k[seq]
+        for t in range(qc):
+            for kb in range(kb0, kb1):
+                key = (qb + t, g, kb)
+                if key in need:
+                    need[key] += 1
+        if part >= 0:
+            assert part not in parts_seen
+            parts_seen.add(part)
+    assert all(v == 1 for v in need.values())
+    assert parts_seen == set(range(nparts))
+    for m in merges:
+        assert m[4] >= 2
+    return plan
+
+
+@pytest.mark.parametrize("H,Hk", [(16, 2), (28, 4)])
+def test_planner_covers_causal_pairs_exactly_once(H, Hk):
+    cu_q = [0, 118, 150, 150 + 300, 150 + 300 + 9]
+    cu_k = [0, 118, 118 + 1072, 118 + 1072 + 300, 118 + 1072 + 300 + 509]
+    _coverage(cu_q, cu_k, H, Hk, num_sms=16)
+
+
+def test_planner_cfg2_balanced():
+    cu_q, cu_k = [0, 1075, 1123], [0, 1075, 11692]
+    plan = _coverage(cu_q, cu_k, 16, 2, num_sms=148)
+    grid, cta, units, merges, _ = _decode_plan(plan)
+    loads = [units[cta[i]:cta[i + 1], 9].sum() / 16.0 for i in range(grid)]
+    assert grid == 148 and max(loads) <= 1.5 * np.mean(loads)
+    assert plan.workspace_bytes == plan.num_parts * 128 * 130 * 4
+
+
+def test_planner_rejects_bad_metadata():
+    from vlcache_b200 import ops
+    from vlcache_b200._lib import VLCError
+    with pytest.raises((ValueError, VLCError)):
+        ops.build_prefill_plan([0, 10], [0, 5], 16, 2)      # more queries than keys
+    with pytest.raises((ValueError, VLCError)):
+        ops.build_prefill_plan([1, 10], [0, 20], 16, 2)     # cu_seqlens must start at 0
+    with pytest.raises((ValueError, VLCError)):
+        ops.build_prefill_plan([0, 10], [0, 20], 16, 3)     # heads not divisible
+
+
+def test_planner_empty_and_zero_length():
+    from vlcache_b200 import ops
+    plan = ops.build_prefill_plan([0, 0, 5], [0, 7, 12], 16, 2, num_sms=8)
+    grid, cta, units, merges, _ = _decode_plan(plan)
+    assert len(units) == 2 and all(int(u[0]) == 1 for u in units)
+    plan = ops.build_prefill_plan([0], [0], 16, 2, num_sms=8)
+    assert plan.grid == 0
+
+
+def test_ops_reject_cpu_tensors():
+    """The product has no CPU path: CPU tensors fail loudly instead of silently falling back."""
+    from vlcache_b200 import ops
+    k = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(2, 256, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.store_kvcache(k, k, kc, kc, torch.zeros(4, dtype=torch.int32))

@@ -1,0 +1,193 @@
+// KV-cache row kernels: the paged scatter (store_kvcache) and the M-RoPE
+// position shift of reused vision K.  Both are HBM-bound row copies done with
+// 128-bit vector loads/stores, one warp-slice per row.
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace vlc {
+
+// ---------------------------------------------------------------------------
+// store_kvcache: k_cache.view(-1, D)[slot[i]] = key[i]  (and V), slot -1 skipped.
+// Semantics of nanovllm/layers/attention.py:10-30 (Triton store_kvcache_kernel).
+// One warp per token; each lane moves 16-byte chunks of the K and V rows.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) store_kvcache_kernel(
+    const uint4* __restrict__ key, int64_t key_stride16, const uint4* __restrict__ value,
+    int64_t value_stride16, uint4* __restrict__ k_cache, uint4* __restrict__ v_cache,
+    const int32_t* __restrict__ slot_mapping, int num_tokens, int chunks_per_row,
+    int64_t num_slots) {
+  const int token = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (token >= num_tokens) return;
+  const int lane = threadIdx.x & 31;
+  const int slot = __ldg(slot_mapping + token);
+  if (slot == -1) return;
+  if (slot < -1 || (int64_t)slot >= num_slots) {
+    if (lane == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
+    return;
+  }
+  const uint4* ks = key + (int64_t)token * key_stride16;
+  const uint4* vs = value + (int64_t)token * value_stride16;
+  uint4* kd = k_cache + (int64_t)slot * chunks_per_row;
+  uint4* vd = v_cache + (int64_t)slot * chunks_per_row;
+  for (int c = lane; c < chunks_per_row; c += 32) {
+    const uint4 kv = __ldg(ks + c);
+    const uint4 vv = __ldg(vs + c);
+    kd[c] = kv;
+    vd[c] = vv;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// M-RoPE shift.  Rotate-half pairs (j, j+half): a K row stored rotated at
+// position p is re-rotated by the per-section delta d_sec(j):
+//   y1 = x1*cos(a_j) - x2*sin(a_j),  y2 = x2*cos(a_j) + x1*sin(a_j),
+//   a_j = inv_freq[j] * d_sec(j)
+// which equals the rotation at p + d because R(a+b) = R(b) R(a) per pair.
+// Thread = one head x 8 consecutive pairs (two 16-byte loads); V rows are
+// copied with the same threads when moving rows to new slots.
+// ---------------------------------------------------------------------------
+constexpr int kMaxHalf = 128;
+struct RopeTable {
+  float c[kMaxHalf];
+  float s[kMaxHalf];
+};
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(f[0], f[1]);
+  u.y = pack_bf16x2(f[2], f[3]);
+  u.z = pack_bf16x2(f[4], f[5]);
+  u.w = pack_bf16x2(f[6], f[7]);
+  return u;
+}
+
+__global__ void __launch_bounds__(256) mrope_shift_kernel(
+    __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+    int64_t layer_stride, int64_t num_slots, int num_kv_heads, int head_dim,
+    const int32_t* __restrict__ src_slots, const int32_t* __restrict__ dst_slots, int num_rows,
+    const __grid_constant__ RopeTable tab) {
+  const int half = head_dim >> 1;
+  const int chunks_per_head = half >> 3;  // 8 pairs per thread
+  const int threads_per_row = num_kv_heads * chunks_per_head;
+  const int rows_per_block = blockDim.x / threads_per_row;
+  const int r_local = threadIdx.x / threads_per_row;
+  const int t = threadIdx.x - r_local * threads_per_row;
+  if (r_local >= rows_per_block) return;
+  const int row = blockIdx.x * rows_per_block + r_local;
+  if (row >= num_rows) return;
+  const int layer = blockIdx.y;
+
+  const int src = __ldg(src_slots + row);
+  const int dst = dst_slots ? __ldg(dst_slots + row) : src;
+  if (src < 0 || dst < 0 || (int64_t)src >= num_slots || (int64_t)dst >= num_slots) {
+    if (t == 0 && layer == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
+    return;
+  }
+  const int head = t / chunks_per_head;
+  const int c = t - head * chunks_per_head;
+  const int64_t row_elems = (int64_t)num_kv_heads * head_dim;
+  const int64_t lbase = (int64_t)layer * layer_stride;
+  const int64_t so = lbase + (int64_t)src * row_elems + (int64_t)head * head_dim + c * 8;
+  const int64_t dof = lbase + (int64_t)dst * row_elems + (int64_t)head * head_dim + c * 8;
+
+  const uint4 u1 = *reinterpret_cast<const uint4*>(k_cache + so);
+  const uint4 u2 = *reinterpret_cast<const uint4*>(k_cache + so + half);
+  float x1[8], x2[8], y1[8], y2[8];
+  unpack8(u1, x1);
+  unpack8(u2, x2);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float cs = tab.c[c * 8 + i];
+    const float sn = tab.s[c * 8 + i];
+    const float t1 = __fmul_rn(x2[i], sn);
+    const float t2 = __fmul_rn(x1[i], sn);
+    y1[i] = __fmaf_rn(x1[i], cs, -t1);
+    y2[i] = __fmaf_rn(x2[i], cs, t2);
+  }
+  *reinterpret_cast<uint4*>(k_cache + dof) = pack8(y1);
+  *reinterpret_cast<uint4*>(k_cache + dof + half) = pack8(y2);
+
+  if (v_cache != nullptr && dst_slots != nullptr) {
+    // Same thread copies the two matching 16-byte chunks of the V row.
+    const uint4 w1 = *reinterpret_cast<const uint4*>(v_cache + so);
+    const uint4 w2 = *reinterpret_cast<const uint4*>(v_cache + so + half);
+    *reinterpret_cast<uint4*>(v_cache + dof) = w1;
+    *reinterpret_cast<uint4*>(v_cache + dof + half) = w2;
+  }
+}
+
+// inv_freq[j] in fp32 exactly as the RoPE reference builds it:
+//   1 / (theta ** (float(2j) / float(dim)))
+static float inv_freq_f32(float theta, int j, int head_dim) {
+  const float e = (float)(2 * j) / (float)head_dim;
+  const float p = powf(theta, e);
+  return 1.0f / p;
+}
+
+}  // namespace vlc
+
+using namespace vlc;
+
+extern "C" int vlc_store_kvcache(const void* key, int64_t key_stride, const void* value,
+                                 int64_t value_stride, void* k_cache, void* v_cache,
+                                 const int32_t* slot_mapping, int num_tokens, int row_elems,
+                                 int64_t num_slots, void* stream) {
+  if (num_tokens < 0 || row_elems <= 0) return VLC_ERR_SHAPE;
+  if (num_tokens == 0) return VLC_OK;
+  if (!key || !value || !k_cache || !v_cache || !slot_mapping) return VLC_ERR_NULL;
+  if (row_elems % 8 != 0 || key_stride % 8 != 0 || value_stride % 8 != 0) return VLC_ERR_STRIDE;
+  if (key_stride < row_elems || value_stride < row_elems) return VLC_ERR_STRIDE;
+  if (!aligned16(key) || !aligned16(value) || !aligned16(k_cache) || !aligned16(v_cache))
+    return VLC_ERR_ALIGN;
+  const int warps = 8;
+  dim3 grid((num_tokens + warps - 1) / warps);
+  store_kvcache_kernel<<<grid, warps * 32, 0, (cudaStream_t)stream>>>(
+      (const uint4*)key, key_stride / 8, (const uint4*)value, value_stride / 8, (uint4*)k_cache,
+      (uint4*)v_cache, slot_mapping, num_tokens, row_elems / 8, num_slots);
+  return launch_status();
+}
+
+extern "C" int vlc_mrope_shift(void* k_cache, void* v_cache, int64_t layer_stride, int num_layers,
+                               int64_t num_slots, int num_kv_heads, int head_dim,
+                               const int32_t* src_slots, const int32_t* dst_slots, int num_rows,
+                               const int32_t* delta_thw, const int32_t* mrope_section,
+                               float rope_theta, void* stream) {
+  if (num_rows < 0 || num_layers < 0) return VLC_ERR_SHAPE;
+  if (num_rows == 0 || num_layers == 0) return VLC_OK;
+  if (!k_cache || !src_slots || !delta_thw || !mrope_section) return VLC_ERR_NULL;
+  if (head_dim % 16 != 0 || head_dim / 2 > kMaxHalf || num_kv_heads <= 0) return VLC_ERR_UNSUPPORTED;
+  const int half = head_dim / 2;
+  if (mrope_section[0] < 0 || mrope_section[1] < 0 || mrope_section[2] < 0 ||
+      mrope_section[0] + mrope_section[1] + mrope_section[2] != half)
+    return VLC_ERR_SHAPE;
+  const int threads_per_row = num_kv_heads * (half / 8);
+  if (threads_per_row > 256) return VLC_ERR_UNSUPPORTED;
+  if (!aligned16(k_cache) || (v_cache && !aligned16(v_cache))) return VLC_ERR_ALIGN;
+  if (num_layers > 1 && (layer_stride % 8 != 0 || layer_stride < num_slots * num_kv_heads * head_dim))
+    return VLC_ERR_STRIDE;
+  RopeTable tab;
+  for (int j = 0; j < half; ++j) {
+    const int sec = j < mrope_section[0] ? 0 : (j < mrope_section[0] + mrope_section[1] ? 1 : 2);
+    const double a = (double)inv_freq_f32(rope_theta, j, head_dim) * (double)delta_thw[sec];
+    tab.c[j] = (float)cos(a);
+    tab.s[j] = (float)sin(a);
+  }
+  const int rows_per_block = 256 / threads_per_row;
+  dim3 grid((num_rows + rows_per_block - 1) / rows_per_block, num_layers);
+  mrope_shift_kernel<<<grid, rows_per_block * threads_per_row, 0, (cudaStream_t)stream>>>(
+      (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, layer_stride, num_slots, num_kv_heads,
+      head_dim, src_slots, dst_slots, num_rows, tab);
+  return launch_status();
+}

@@ -1,0 +1,234 @@
+"""Torch-facing wrappers over the C ABI (device pointers, strides, current stream).
+
+These are thin: validate what the reference validates, hand raw pointers to the
+library, raise on a non-zero status.  Every op runs its CUDA kernel; tensors on
+the CPU are rejected (there is no CPU path in the product).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._lib import check, lib
+
+HEAD_DIM = 128
+DEFAULT_MROPE_SECTION = (16, 24, 24)  # Qwen2.5-VL rope_scaling.mrope_section
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("vlcache_b200 ops run on CUDA tensors only (no CPU fallback)")
+
+
+def num_sms() -> int:
+    return int(lib().vlc_num_sms())
+
+
+def device_error(reset: bool = True) -> int:
+    """Synchronise and return (and by default clear) the library's device error word."""
+    return int(lib().vlc_get_device_error(1 if reset else 0))
+
+
+# --------------------------------------------------------------------------- scatter
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """``k_cache.view(-1, D)[slot_mapping[i]] = key[i]`` (and V); slot -1 is skipped.
+
+    Same contract and assertions as nanovllm/layers/attention.py:33-40.
+    """
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    assert key.stride(-1) == 1 and value.stride(-1) == 1
+    assert key.stride(1) == head_dim and value.stride(1) == head_dim
+    assert k_cache.stride(1) == D and v_cache.stride(1) == D
+    assert slot_mapping.numel() == N
+    _require_cuda(key, value, k_cache, v_cache, slot_mapping)
+    assert key.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16
+    assert slot_mapping.dtype == torch.int32
+    num_slots = k_cache.numel() // D
+    st = lib().vlc_store_kvcache(_ptr(key), key.stride(0), _ptr(value), value.stride(0), _ptr(k_cache),
+                                 _ptr(v_cache), _ptr(slot_mapping), N, D, num_slots, _stream())
+    check("vlc_store_kvcache", st)
+
+
+# --------------------------------------------------------------------------- M-RoPE shift
+def mrope_shift(k_cache: torch.Tensor, v_cache: torch.Tensor | None, src_slots: torch.Tensor,
+                dst_slots: torch.Tensor | None, delta_thw, mrope_section=DEFAULT_MROPE_SECTION,
+                rope_theta: float = 1e6) -> None:
+    """Re-rotate reused K rows of one layer by an M-RoPE position delta.
+
+    ``k_cache``/``v_cache`` are one layer's ``[num_blocks, block_size, Hk, D]`` (or
+    ``[num_slots, Hk, D]``) caches.  With ``dst_slots`` None the rotation is in place;
+    otherwise K rows move (rotated) to ``dst_slots`` and V rows move verbatim.
+    """
+    _require_cuda(k_cache, v_cache, src_slots, dst_slots)
+    assert k_cache.dtype == torch.bfloat16 and k_cache.is_contiguous()
+    assert src_slots.dtype == torch.int32 and (dst_slots is None or dst_slots.dtype == torch.int32)
+    Hk, hd = k_cache.shape[-2], k_cache.shape[-1]
+    num_slots = k_cache.numel() // (Hk * hd)
+    n = src_slots.numel()
+    if dst_slots is not None:
+        assert dst_slots.numel() == n
+    d = (ctypes.c_int32 * 3)(*[int(x) for x in delta_thw])
+    sec = (ctypes.c_int32 * 3)(*[int(x) for x in mrope_section])
+    st = lib().vlc_mrope_shift(_ptr(k_cache), _ptr(v_cache), 0, 1, int(num_slots), int(Hk), int(hd),
+                               _ptr(src_slots), _ptr(dst_slots), n, d, sec, float(rope_theta), _stream())
+    check("vlc_mrope_shift", st)
+
+
+def mrope_shift_all_layers(kv_cache: torch.Tensor, src_slots: torch.Tensor, dst_slots: torch.Tensor | None,
+                           delta_thw, mrope_section=DEFAULT_MROPE_SECTION, rope_theta: float = 1e6) -> None:
+    """Shift reused image rows of every layer of a ``[2, L, NB, BS, Hk, D]`` cache in one launch."""
+    assert kv_cache.dim() == 6 and kv_cache.is_contiguous()
+    L = kv_cache.shape[1]
+    per_layer = kv_cache[0, 0].numel()
+    k0 = kv_cache[0, 0]
+    v0 = kv_cache[1, 0]
+    Hk, hd = kv_cache.shape[4], kv_cache.shape[5]
+    num_slots = kv_cache.shape[2] * kv_cache.shape[3]
+    _require_cuda(kv_cache, src_slots, dst_slots)
+    n = src_slots.numel()
+    d = (ctypes.c_int32 * 3)(*[int(x) for x in delta_thw])
+    sec = (ctypes.c_int32 * 3)(*[int(x) for x in mrope_section])
+    st = lib().vlc_mrope_shift(_ptr(k0), _ptr(v0) if dst_slots is not None else ctypes.c_void_p(0),
+                               per_layer, L, num_slots, Hk, hd, _ptr(src_slots), _ptr(dst_slots), n, d, sec,
+                               float(rope_theta), _stream())
+    check("vlc_mrope_shift", st)
+
+
+# --------------------------------------------------------------------------- prefill
+@dataclass
+class PrefillPlan:
+    """Host plan (numpy int32) plus its device copy and workspace size (bytes)."""
+    host: np.ndarray
+    dev: torch.Tensor | None
+    workspace_bytes: int
+
+    @property
+    def grid(self) -> int:
+        return int(self.host[2])
+
+    @property
+    def num_units(self) -> int:
+        return int(self.host[3])
+
+    @property
+    def num_parts(self) -> int:
+        return int(self.host[4])
+
+    @property
+    def num_merges(self) -> int:
+        return int(self.host[5])
+
+
+def build_prefill_plan(cu_seqlens_q, cu_seqlens_k, num_heads: int, num_kv_heads: int, head_dim: int = HEAD_DIM,
+                       num_sms: int = 0, device: torch.device | str | None = None) -> PrefillPlan:
+    """Plan the warm-prefill attention launch from HOST cu_seqlens (lists/arrays/CPU tensors)."""
+    cq = np.ascontiguousarray(np.asarray(cu_seqlens_q, dtype=np.int32))
+    ck = np.ascontiguousarray(np.asarray(cu_seqlens_k, dtype=np.int32))
+    nseq = len(cq) - 1
+    assert len(ck) == nseq + 1
+    L = lib()
+    sms = int(num_sms) if num_sms else (L.vlc_num_sms() if device is not None else 148)
+    cap = L.vlc_prefill_plan_capacity(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads, sms)
+    if cap < 0:
+        raise ValueError("invalid prefill metadata (cu_seqlens / heads)")
+    plan = np.zeros(int(cap), dtype=np.int32)
+    used = ctypes.c_int64(0)
+    st = L.vlc_prefill_plan(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads, head_dim, sms,
+                            plan.ctypes.data, int(cap), ctypes.byref(used))
+    check("vlc_prefill_plan", st)
+    plan = plan[: used.value].copy()
+    ws = int(L.vlc_prefill_workspace_size(plan.ctypes.data))
+    dev = None
+    if device is not None:
+        dev = torch.from_numpy(plan).pin_memory().to(device, non_blocking=True)
+    return PrefillPlan(host=plan, dev=dev, workspace_bytes=ws)
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_tables: torch.Tensor | None,
+                      plan: PrefillPlan, softmax_scale: float, out: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal (bottom-right) varlen attention — the flash_attn_varlen_func contract.
+
+    Paged: ``k``/``v`` are one layer's ``[num_blocks, block_size, Hk, D]`` caches and
+    ``block_tables`` maps sequences to pages.  Contiguous (``block_tables`` None): ``k``/``v``
+    are ``[total_k, Hk, D]`` (any token stride) laid out by cu_seqlens_k.
+    """
+    _require_cuda(q, k, v, block_tables)
+    assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+    total_q, H, hd = q.shape
+    assert q.stride(2) == 1 and q.stride(1) == hd
+    Hk = k.shape[-2]
+    assert k.stride(-1) == 1 and k.stride(-2) == hd and v.stride(-1) == 1 and v.stride(-2) == hd
+    if block_tables is not None:
+        assert k.dim() == 4 and k.is_contiguous() and v.is_contiguous()
+        block_size = k.shape[1]
+        rows = k.shape[0] * k.shape[1]
+        k_stride = v_stride = Hk * hd
+        assert block_tables.dtype == torch.int32 and block_tables.stride(-1) == 1
+        bt_ptr, bt_stride = _ptr(block_tables), block_tables.stride(0)
+    else:
+        assert k.dim() == 3 and v.dim() == 3 and k.shape[0] == v.shape[0]
+        block_size, rows = 0, k.shape[0]
+        k_stride, v_stride = k.stride(0), v.stride(0)
+        bt_ptr, bt_stride = ctypes.c_void_p(0), 0
+    if out is None:
+        out = torch.empty(total_q, H, hd, dtype=q.dtype, device=q.device)
+    assert out.stride(2) == 1 and out.stride(1) == hd
+    if plan.dev is None or plan.dev.device != q.device:
+        plan.dev = torch.from_numpy(plan.host).to(q.device)
+    if plan.workspace_bytes > 0 and (workspace is None or workspace.numel() * workspace.element_size()
+                                     < plan.workspace_bytes):
+        workspace = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = lib().vlc_prefill_attn(_ptr(q), q.stride(0), total_q, H, _ptr(k), _ptr(v), k_stride, v_stride, rows,
+                                Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev), plan.host.ctypes.data,
+                                float(softmax_scale), _ptr(out), out.stride(0), _ptr(workspace), ws_bytes,
+                                _stream())
+    check("vlc_prefill_attn", st)
+    return out
+
+
+# --------------------------------------------------------------------------- decode
+def decode_workspace_bytes(num_seqs: int, num_heads: int, num_kv_heads: int, max_context_len: int) -> int:
+    return int(lib().vlc_decode_workspace_size(num_seqs, num_heads, num_kv_heads, max_context_len))
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                     context_lens: torch.Tensor, max_context_len: int, softmax_scale: float,
+                     out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One-token paged decode (flash_attn_with_kvcache contract); q/out are ``[B, H, D]``."""
+    _require_cuda(q, k_cache, v_cache, block_tables, context_lens)
+    if q.dim() == 4:
+        q = q.squeeze(1)
+    B, H, hd = q.shape
+    assert q.stride(2) == 1 and q.stride(1) == hd
+    Hk = k_cache.shape[-2]
+    block_size = k_cache.shape[1] if k_cache.dim() == 4 else 256
+    num_slots = k_cache.numel() // (Hk * hd)
+    assert context_lens.dtype == torch.int32 and block_tables.dtype == torch.int32
+    if out is None:
+        out = torch.empty(B, H, hd, dtype=q.dtype, device=q.device)
+    need = decode_workspace_bytes(B, H, Hk, max_context_len)
+    if need > 0 and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    st = lib().vlc_decode_attn(_ptr(q), q.stride(0), B, H, _ptr(k_cache), _ptr(v_cache), num_slots, Hk, hd,
+                               _ptr(block_tables), block_tables.stride(0), block_size, _ptr(context_lens),
+                               int(max_context_len), float(softmax_scale), _ptr(out), out.stride(0),
+                               _ptr(workspace), ws_bytes, _stream())
+    check("vlc_decode_attn", st)
+    return out
