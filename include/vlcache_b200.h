@@ -157,6 +157,28 @@ int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs, int num_h
 int64_t vlc_decode_workspace_size(int num_seqs, int num_heads, int num_kv_heads,
                                   int max_context_len);
 
+/* --------------------------------------------------------------------------
+ * Decode that allocates nothing.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory (a runtime with a fixed memory budget,
+ * a process that may not call cudaMalloc after start-up).  Same arguments and
+ * result as vlc_decode_attn minus the workspace: the split partials go to a
+ * library-owned device array of vlc_decode_noalloc_scratch_bytes() (8 MiB) that
+ * every GPU loading the library holds until exit.  Requests needing more
+ * (vlc_decode_workspace_size() larger than that) return VLC_ERR_WORKSPACE without
+ * launching.  Calls on one device share the array: calls that overlap on the GPU
+ * race.  The first call on each device looks up the array's device address; make
+ * it before any stream capture.
+ * ------------------------------------------------------------------------ */
+int vlc_decode_attn_noalloc(const void* q, int64_t q_seq_stride, int num_seqs, int num_heads,
+                            const void* k_cache, const void* v_cache, int64_t num_slots,
+                            int num_kv_heads, int head_dim, const int32_t* block_tables,
+                            int block_table_stride, int block_size, const int32_t* context_lens,
+                            int max_context_len, float softmax_scale, void* out,
+                            int64_t out_seq_stride, void* stream);
+
+/* Size in bytes of the built-in scratch array used by vlc_decode_attn_noalloc. */
+int64_t vlc_decode_noalloc_scratch_bytes(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,9 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_decode_attn": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_int, c_int, c_vp, c_int,
                                 c_int, c_vp, c_int, c_float, c_vp, c_i64, c_vp, c_i64, c_vp]),
     "vlc_decode_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),
+    "vlc_decode_attn_noalloc": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_int, c_int, c_vp, c_int,
+                                        c_int, c_vp, c_int, c_float, c_vp, c_i64, c_vp]),
+    "vlc_decode_noalloc_scratch_bytes": (c_i64, []),
 }
 
 

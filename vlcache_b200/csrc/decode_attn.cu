@@ -15,6 +15,7 @@
 // device and CTAs past a sequence's last split exit immediately.
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -498,4 +499,77 @@ extern "C" int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs
   decode_combine_kernel<<<cg, 128, 0, st>>>(prm.part_o, prm.part_ml, context_lens, sk, max_splits, num_heads,
                                            prm.out, out_seq_stride);
   return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Decode without any device allocation.
+//
+// Some callers cannot allocate device memory at all: a runtime that hands this
+// library a fixed memory budget up front, a host process that is not allowed to
+// call cudaMalloc after start-up, or code running where an allocation could block
+// or fail at a bad time.  For them the split-K partial results live in one
+// file-scope device array that is part of the library image, so every GPU that
+// loads the library holds it until the process exits.
+//
+//   * Limit: kNoAllocScratchBytes (8 MiB).  A request whose split partials need more
+//     (vlc_decode_workspace_size() > 8 MiB) is rejected with VLC_ERR_WORKSPACE before
+//     anything is launched.
+//   * Nothing in the array has to start at zero: every split that the combine step
+//     reads is written by the same call first.  The array keeps the last call's
+//     contents.
+//   * All calls on a device share the one array: two calls whose kernels overlap on
+//     the GPU (different streams, or different host threads) race on it.  Serialise
+//     them, e.g. on one stream.
+//   * Host code cannot use the array's name as a device address; its address is
+//     fetched once per device with cudaGetSymbolAddress by the first call made while
+//     that device is current.  Make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace vlc {
+namespace decode {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VLC_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return VLC_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return VLC_OK;
+}
+
+}  // namespace decode
+}  // namespace vlc
+
+extern "C" int64_t vlc_decode_noalloc_scratch_bytes(void) { return vlc::decode::kNoAllocScratchBytes; }
+
+extern "C" int vlc_decode_attn_noalloc(const void* q, int64_t q_seq_stride, int num_seqs, int num_heads,
+                                       const void* k_cache, const void* v_cache, int64_t num_slots,
+                                       int num_kv_heads, int head_dim, const int32_t* block_tables,
+                                       int block_table_stride, int block_size, const int32_t* context_lens,
+                                       int max_context_len, float softmax_scale, void* out,
+                                       int64_t out_seq_stride, void* stream) {
+  const int64_t need = vlc_decode_workspace_size(num_seqs, num_heads, num_kv_heads, max_context_len);
+  if (need > vlc::decode::kNoAllocScratchBytes) return VLC_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = vlc::decode::noalloc_scratch(&scratch);
+    if (rc != VLC_OK) return rc;
+  }
+  return vlc_decode_attn(q, q_seq_stride, num_seqs, num_heads, k_cache, v_cache, num_slots, num_kv_heads,
+                         head_dim, block_tables, block_table_stride, block_size, context_lens, max_context_len,
+                         softmax_scale, out, out_seq_stride, scratch,
+                         need > 0 ? vlc::decode::kNoAllocScratchBytes : 0, stream);
 }
