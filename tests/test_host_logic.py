@@ -55,14 +55,26 @@ def test_recompute_count():
 
 
 # ---------------------------------------------------------------- planner (C ABI, host only)
+UNIT_INTS, MERGE_INTS = 16, 8
+
+
 def _decode_plan(plan):
     from vlcache_b200 import ops  # noqa: F401  (loads the library)
     h = plan.host
     grid, nu, nparts, nm = int(h[2]), int(h[3]), int(h[4]), int(h[5])
     cta = h[int(h[12]):int(h[12]) + grid + 1]
-    units = h[int(h[13]):int(h[13]) + nu * 12].reshape(nu, 12)
-    merges = h[int(h[14]):int(h[14]) + nm * 8].reshape(nm, 8)
+    units = h[int(h[13]):int(h[13]) + nu * UNIT_INTS].reshape(nu, UNIT_INTS)
+    merges = h[int(h[14]):int(h[14]) + nm * MERGE_INTS].reshape(nm, MERGE_INTS)
     return grid, cta, units, merges, nparts
+
+
+def _unit_tiles(u):
+    """(q_begin, q_count, kpos0, part, kb_begin, kb_end) of the tiles of a unit."""
+    seq, g, kb0, kb1, kvl, kbase, cost = [int(x) for x in u[:7]]
+    out = [(int(u[7]), int(u[8]), int(u[9]), int(u[10]), kb0, kb1)]
+    if int(u[12]) > 0:
+        out.append((int(u[11]), int(u[12]), int(u[13]), int(u[14]), kb0, int(u[15])))
+    return out
 
 
 def _coverage(cu_q, cu_k, H, Hk, num_sms):
@@ -85,17 +97,23 @@ def _coverage(cu_q, cu_k, H, Hk, num_sms):
                     need[(cu_q[b] + t, g, kb)] = 0
     parts_seen = set()
     for u in units:
-        seq, g, qb, qc, kp0, kb0, kb1, kvl, part = [int(x) for x in u[:9]]
-        assert 1 <= qc <= T and kb0 < kb1
-        assert kvl == cu_k[seq + 1] - cu_k[seq] and int(u[10]) == cu_k[seq]
-        for t in range(qc):
-            for kb in range(kb0, kb1):
-                key = (qb + t, g, kb)
-                if key in need:
-                    need[key] += 1
-        if part >= 0:
-            assert part not in parts_seen
-            parts_seen.add(part)
+        seq, g = int(u[0]), int(u[1])
+        assert int(u[4]) == cu_k[seq + 1] - cu_k[seq] and int(u[5]) == cu_k[seq]
+        tiles = _unit_tiles(u)
+        assert tiles[0][5] > tiles[0][4]                    # tile A always has work
+        if len(tiles) == 2:
+            assert tiles[1][0] + tiles[1][1] <= tiles[0][0]  # B holds the earlier tokens
+            assert tiles[1][5] <= tiles[0][5]
+        for (qb, qc, kp0, part, kb0, kb1) in tiles:
+            assert 1 <= qc <= T
+            for t in range(qc):
+                for kb in range(kb0, kb1):
+                    key = (qb + t, g, kb)
+                    if key in need:
+                        need[key] += 1
+            if part >= 0:
+                assert part not in parts_seen
+                parts_seen.add(part)
     assert all(v == 1 for v in need.values())
     assert parts_seen == set(range(nparts))
     for m in merges:
@@ -114,9 +132,9 @@ def test_planner_cfg2_balanced():
     cu_q, cu_k = [0, 1075, 1123], [0, 1075, 11692]
     plan = _coverage(cu_q, cu_k, 16, 2, num_sms=148)
     grid, cta, units, merges, _ = _decode_plan(plan)
-    loads = [units[cta[i]:cta[i + 1], 9].sum() / 16.0 for i in range(grid)]
-    assert grid == 148 and max(loads) <= 1.5 * np.mean(loads)
-    assert plan.workspace_bytes == plan.num_parts * 128 * 130 * 4
+    loads = [units[cta[i]:cta[i + 1], 6].sum() / 16.0 for i in range(grid)]
+    assert grid == 148 and max(loads) <= 1.6 * np.mean(loads)
+    assert plan.workspace_bytes == plan.num_parts * 128 * (128 * 2 + 8)
 
 
 def test_planner_rejects_bad_metadata():
@@ -134,7 +152,7 @@ def test_planner_empty_and_zero_length():
     from vlcache_b200 import ops
     plan = ops.build_prefill_plan([0, 0, 5], [0, 7, 12], 16, 2, num_sms=8)
     grid, cta, units, merges, _ = _decode_plan(plan)
-    assert len(units) == 2 and all(int(u[0]) == 1 for u in units)
+    assert len(units) == 2 and all(int(u[0]) == 1 for u in units)   # one single-tile unit per KV head
     plan = ops.build_prefill_plan([0], [0], 16, 2, num_sms=8)
     assert plan.grid == 0
 

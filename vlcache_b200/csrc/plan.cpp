@@ -1,18 +1,19 @@
 // Host planner for the warm-prefill attention kernel.
 //
-// Builds the list of work units (query tile x key-block range) from the
-// varlen metadata the nano-vllm model runner produces
-// (nanovllm/engine/model_runner.py:194-320 prepare_prefill: cu_seqlens_q,
-// cu_seqlens_k with bottom-right causal alignment) and bin-packs them onto a
-// persistent grid of one CTA per SM (longest-processing-time first).  Rows
-// whose key range is long (text after the image sees the whole image) are split
-// into several units so the per-CTA work is balanced; their partial results
-// are merged by a second small kernel.
+// Builds the list of work units from the varlen metadata the nano-vllm model
+// runner produces (nanovllm/engine/model_runner.py:194-320 prepare_prefill:
+// cu_seqlens_q, cu_seqlens_k with bottom-right causal alignment) and bin-packs
+// them onto a persistent grid of one CTA per SM (longest-processing-time first).
+// A unit is one query tile over one range of 128-key blocks.  Tiles whose key
+// range is long (text after the image sees the whole image) are split into
+// several units so the per-CTA work is balanced; the partial results are merged
+// by a second small kernel.
 //
 // Pure host code (the only CUDA query is the SM count when num_sms == 0, which
 // falls back to 148 without a device): usable without a GPU.
 #include <algorithm>
 #include <array>
+#include <cmath>
 #include <cstdint>
 #include <queue>
 #include <vector>
@@ -103,47 +104,57 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   std::vector<Tile> tiles;
   build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, tiles);
 
-  int64_t total_kb = 0;
-  for (const Tile& t : tiles) total_kb += t.n_kb;
-  // Split long tiles so no unit is much longer than the per-SM average.
-  const int64_t avg = (total_kb + num_sms - 1) / std::max(1, num_sms);
-  const int chunk = (int)std::max<int64_t>(4, avg);
-  const double kUnitOverhead = 1.0;   // Q load + epilogue, in K-tile units
-  const double kPartOverhead = 0.5;   // fp32 partial write + merge share
-
+  // Time model (in key-block iterations of one tile): each unit pays a fixed
+  // start/epilogue cost, each split part a partial write and its share of the merge.
+  const double kUnitOverhead = 1.5, kPartOverhead = 0.5;
+  double total_time = 0.0;
+  for (const Tile& t : tiles) total_time += t.n_kb + kUnitOverhead;
+  const double avg = total_time / std::max(1, num_sms);
+  // Split only tiles well above the per-SM average, into parts of about the average.
+  const double split_above = std::max(4.0, 1.5 * avg);
+  const double target = std::max(3.0, avg);
   std::vector<UnitRec> units;
   std::vector<std::array<int32_t, kMergeInts>> merges;
   int num_parts = 0;
-  for (const Tile& t : tiles) {
-    const int np = t.n_kb > chunk ? (t.n_kb + chunk - 1) / chunk : 1;
+  auto add_merge = [&](const Tile& t, int part0, int np) {
+    std::array<int32_t, kMergeInts> m{};
+    m[kMQBegin] = t.q_begin;
+    m[kMQCount] = t.q_count;
+    m[kMKvHead] = t.kv_head;
+    m[kMPartBegin] = part0;
+    m[kMNumParts] = np;
+    merges.push_back(m);
+  };
+  for (const Tile& ta : tiles) {
+    int np = ta.n_kb + kUnitOverhead > split_above ? (int)std::ceil(ta.n_kb / target) : 1;
+    np = std::max(1, std::min(np, ta.n_kb));
+    const int part0 = np > 1 ? num_parts : -1;
     if (np > 1) {
-      std::array<int32_t, kMergeInts> m{};
-      m[kMQBegin] = t.q_begin;
-      m[kMQCount] = t.q_count;
-      m[kMKvHead] = t.kv_head;
-      m[kMPartBegin] = num_parts;
-      m[kMNumParts] = np;
-      merges.push_back(m);
+      add_merge(ta, part0, np);
+      num_parts += np;
     }
     for (int i = 0; i < np; ++i) {
       UnitRec u{};
-      const int kb0 = (int)((int64_t)t.n_kb * i / np);
-      const int kb1 = (int)((int64_t)t.n_kb * (i + 1) / np);
-      u.f[kUSeq] = t.seq;
-      u.f[kUKvHead] = t.kv_head;
-      u.f[kUQBegin] = t.q_begin;
-      u.f[kUQCount] = t.q_count;
-      u.f[kUKpos0] = t.kpos0;
+      for (int k = 0; k < kUnitInts; ++k) u.f[k] = 0;
+      const int kb0 = (int)((int64_t)ta.n_kb * i / np);
+      const int kb1 = (int)((int64_t)ta.n_kb * (i + 1) / np);
+      u.f[kUSeq] = ta.seq;
+      u.f[kUKvHead] = ta.kv_head;
       u.f[kUKbBegin] = kb0;
       u.f[kUKbEnd] = kb1;
-      u.f[kUKvLen] = t.kv_len;
-      u.f[kUKBase] = t.k_base;
-      u.f[kUPart] = np > 1 ? num_parts + i : -1;
+      u.f[kUKvLen] = ta.kv_len;
+      u.f[kUKBase] = ta.k_base;
+      u.f[kUQBeginA] = ta.q_begin;
+      u.f[kUQCountA] = ta.q_count;
+      u.f[kUKpos0A] = ta.kpos0;
+      u.f[kUPartA] = np > 1 ? part0 + i : -1;
+      u.f[kUQCountB] = 0;  // single-tile units (tile B fields unused)
+      u.f[kUPartB] = -1;
+      u.f[kUKbEndB] = kb0;
       u.cost = (kb1 - kb0) + kUnitOverhead + (np > 1 ? kPartOverhead : 0.0);
       u.f[kUCost] = (int32_t)(u.cost * 16);
       units.push_back(u);
     }
-    if (np > 1) num_parts += np;
   }
 
   const int num_units = (int)units.size();

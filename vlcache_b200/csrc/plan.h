@@ -8,7 +8,7 @@
 namespace vlc {
 
 constexpr int32_t kPlanMagic = 0x564C4350;  // 'VLCP'
-constexpr int32_t kPlanVersion = 1;
+constexpr int32_t kPlanVersion = 3;
 constexpr int kPlanHeaderInts = 16;
 
 // header fields
@@ -31,23 +31,30 @@ enum : int {
   kPTotalLen = 15,
 };
 
-// unit fields
-constexpr int kUnitInts = 12;
+// A unit is one query tile (fields "A") of one (sequence, KV head) over one range
+// of 128-key blocks.  The "B" fields are reserved for a second tile sharing the
+// key range; the current kernel plans single-tile units (kUQCountB == 0).
+constexpr int kUnitInts = 16;
 enum : int {
-  kUSeq = 0,      // row of block_tables
+  kUSeq = 0,       // row of block_tables
   kUKvHead = 1,
-  kUQBegin = 2,   // first query token (absolute row of q)
-  kUQCount = 3,   // valid query tokens in the tile (<= T)
-  kUKpos0 = 4,    // logical position of the first query token
-  kUKbBegin = 5,  // first 128-key block
-  kUKbEnd = 6,    // one past the last 128-key block
-  kUKvLen = 7,    // keys of the sequence
-  kUPart = 8,     // -1: write the normalised output; else partial slot
-  kUCost = 9,     // planner cost estimate (diagnostic)
-  kUKBase = 10,   // first key row of the sequence when K/V are not paged (cu_seqlens_k[seq])
+  kUKbBegin = 2,   // first 128-key block (both tiles)
+  kUKbEnd = 3,     // one past the last block of tile A
+  kUKvLen = 4,     // keys of the sequence
+  kUKBase = 5,     // first key row of the sequence when K/V are not paged
+  kUCost = 6,      // planner cost estimate x16 (diagnostic)
+  kUQBeginA = 7,   // tile A: first query token (absolute row of q)
+  kUQCountA = 8,   //         valid tokens (1..T)
+  kUKpos0A = 9,    //         logical position of its first token
+  kUPartA = 10,    //         -1: write the normalised output; else partial slot
+  kUQBeginB = 11,  // tile B (kUQCountB == 0: no tile B)
+  kUQCountB = 12,
+  kUKpos0B = 13,
+  kUPartB = 14,
+  kUKbEndB = 15,   // one past tile B's last block (kb_begin .. kb_end_b may be empty)
 };
 
-// merge fields
+// merge fields (one record per split query tile)
 constexpr int kMergeInts = 8;
 enum : int {
   kMQBegin = 0,

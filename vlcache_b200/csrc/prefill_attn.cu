@@ -7,19 +7,24 @@
 // Work decomposition (host planner, plan.cpp): a *tile* is T consecutive
 // query tokens of one sequence x the G query heads of one KV head, packed into
 // the 128 rows of a UMMA M=128 tile (row = token*G + head: GQA packing, so one
-// K/V tile feeds G heads).  A *unit* is a tile x a range of 128-key blocks;
-// long rows are split into several units whose partial results are merged by
-// vlc_prefill_merge_kernel.  Units are bin-packed onto a persistent grid.
+// K/V tile feeds G heads).  A *unit* is a tile over a range of 128-key blocks;
+// long ranges are split into several units whose partial results are merged by
+// prefill_merge_kernel.  Units are bin-packed onto a persistent grid of one CTA
+// per SM.
 //
-// CTA roles (192 threads):
-//   warps 0-3  softmax / correction / epilogue: thread i owns tile row i, which
-//              is TMEM lane i (S and O accumulators live in TMEM)
-//   warp  4    TMA producer: Q tile, K/V tiles (128 keys x 128 dims, SW128)
-//   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
-// Pipelines: K/V smem ring (2 stages), two S buffers in TMEM (QK^T of tile
-// j+1 runs while softmax of tile j executes), O accumulated in TMEM.
-// P is written by the softmax threads into smem in the SW128 K-major layout
-// and consumed as the A operand of O += P V (V is an MN-major B operand).
+// CTA roles (320 threads):
+//   warps 0-3  softmax, columns 0-63 of every S row   (thread i: row i = TMEM lane i)
+//   warps 4-7  softmax, columns 64-127 of every S row
+//   warp  8    TMA producer: Q tiles (double-buffered), K/V tiles (2-stage ring)
+//   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
+// TMEM (512 columns): S0 | S1 | O (128 fp32 columns each).  S is double
+// buffered: Q*K^T of key tile j+1 runs while the softmax works on tile j.  Each
+// softmax thread handles half a row (64 values): the two halves exchange their
+// maxima through shared memory once per tile, then write P (bf16 pairs) back
+// over their half of the S buffer, where the next MMA reads it as the A operand
+// of O += P V (V is an MN-major smem operand).  Online softmax in the log2
+// domain with lazy rescaling: the running max moves (and O is rescaled) only
+// when it grows by more than 2^8.
 #include <algorithm>
 #include <cmath>
 
@@ -34,29 +39,34 @@ constexpr int BM = 128;   // tile rows (tokens * group)
 constexpr int BN = 128;   // keys per K/V tile
 constexpr int HD = 128;   // head dim
 constexpr int STAGES = 2; // K/V ring depth
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
 constexpr int HALF_BYTES = BM * 128;          // 128 rows x 128 B (64 bf16)
 constexpr int TILE_BYTES = 2 * HALF_BYTES;    // 32 KB: full 128 x 128 bf16 tile
 
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_Q = 0;                               // 2 buffers
+constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr int OFF_P = OFF_V + STAGES * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + TILE_BYTES;
-// barriers: q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full, o_done
-constexpr int NUM_BARS = 2 + 4 * STAGES + 2 + 2;
+constexpr int OFF_X = OFF_V + STAGES * TILE_BYTES;     // row-max exchange [2 parity][2 halves][128]
+constexpr int OFF_L = OFF_X + 2 * 2 * BM * 4;          // row-sum exchange [2 halves][128]
+constexpr int OFF_BAR = OFF_L + 2 * BM * 4;
+// barriers: q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done,
+//           xchg[2] (half-row maxima, by tile parity), xsum (row sums, per unit)
+constexpr int NUM_BARS = 4 + 4 * STAGES + 5 + 3;
 constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O = 256;
+constexpr uint32_t TMEM_S = 0;     // S buffer b at TMEM_S + 128 b
+constexpr uint32_t TMEM_O = 256;
 
 constexpr uint32_t IDESC_QK = umma_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, 128, false, true);
 
+constexpr int kSoftmaxThreads = 256;
+
 struct Params {
   CUtensorMap tm_q;   // dims {HD, num_heads, total_q}, box {64, G, T}
-  CUtensorMap tm_k;   // dims {HD, Hk, num_slots},   box {64, 1, BN}
+  CUtensorMap tm_k;   // dims {HD, Hk, num_rows},    box {64, 1, BN}
   CUtensorMap tm_v;
   const int32_t* cta_offsets;  // [grid + 1]
   const int32_t* units;        // [num_units][kUnitInts]
@@ -69,34 +79,38 @@ struct Params {
   int64_t num_slots;
   __nv_bfloat16* out;
   int64_t out_token_stride;
-  float* part_o;       // [num_parts][BM][HD] unnormalised
-  float* part_ml;      // [num_parts][BM][2]  (max in log2 domain, sum)
+  __nv_bfloat16* part_o;  // [num_parts][BM][HD] partial O / l (bf16)
+  float* part_ml;         // [num_parts][BM][2]  (max in log2 domain, sum)
 };
 
 struct Bars {
-  uint64_t* q_full;
-  uint64_t* q_empty;
+  uint64_t* q_full;   // [2]
+  uint64_t* q_empty;  // [2]
   uint64_t* k_full;
   uint64_t* k_empty;
   uint64_t* v_full;
   uint64_t* v_empty;
-  uint64_t* s_full;
-  uint64_t* p_full;
+  uint64_t* s_full;   // [2]
+  uint64_t* p_full;   // [2]
   uint64_t* o_done;
+  uint64_t* xchg;     // [2]
+  uint64_t* xsum;
 };
 
 __device__ __forceinline__ Bars make_bars(uint8_t* smem) {
   uint64_t* b = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   Bars r;
   r.q_full = b;
-  r.q_empty = b + 1;
-  r.k_full = b + 2;
-  r.k_empty = b + 2 + STAGES;
-  r.v_full = b + 2 + 2 * STAGES;
-  r.v_empty = b + 2 + 3 * STAGES;
-  r.s_full = b + 2 + 4 * STAGES;
-  r.p_full = b + 4 + 4 * STAGES;
-  r.o_done = b + 5 + 4 * STAGES;
+  r.q_empty = b + 2;
+  r.k_full = b + 4;
+  r.k_empty = b + 4 + STAGES;
+  r.v_full = b + 4 + 2 * STAGES;
+  r.v_empty = b + 4 + 3 * STAGES;
+  r.s_full = b + 4 + 4 * STAGES;
+  r.p_full = b + 6 + 4 * STAGES;
+  r.o_done = b + 8 + 4 * STAGES;
+  r.xchg = b + 9 + 4 * STAGES;
+  r.xsum = b + 11 + 4 * STAGES;
   return r;
 }
 
@@ -134,6 +148,23 @@ __device__ __forceinline__ int key_block_slot(const Params& p, const int32_t* u,
   return (int)slot;
 }
 
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+#pragma unroll
+  for (int k = 0; k < HD / 16; ++k) {
+    const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
+    umma_ss(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), IDESC_QK,
+            k > 0 ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+#pragma unroll
+  for (int k = 0; k < BN / 16; ++k) {
+    umma_ts(o_tmem, p_tmem + k * 8, umma_desc_sw128(v_addr + k * 2048, HALF_BYTES, 1024), IDESC_PV,
+            (accumulate || k > 0) ? 1u : 0u);
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -146,37 +177,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   const int u_begin = __ldg(p.cta_offsets + blockIdx.x);
   const int u_end = __ldg(p.cta_offsets + blockIdx.x + 1);
 
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    mbar_init(bars.q_full, 1);
-    mbar_init(bars.q_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bars.q_full + b, 1);
+      mbar_init(bars.q_empty + b, 1);
+      mbar_init(bars.s_full + b, 1);
+      mbar_init(bars.p_full + b, kSoftmaxThreads);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bars.k_full + s, 1);
       mbar_init(bars.k_empty + s, 1);
       mbar_init(bars.v_full + s, 1);
       mbar_init(bars.v_empty + s, 1);
     }
-    mbar_init(bars.s_full + 0, 1);
-    mbar_init(bars.s_full + 1, 1);
-    mbar_init(bars.p_full, 128);
     mbar_init(bars.o_done, 1);
+    mbar_init(bars.xchg + 0, kSoftmaxThreads);
+    mbar_init(bars.xchg + 1, kSoftmaxThreads);
+    mbar_init(bars.xsum, kSoftmaxThreads);
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
   }
-  // Rows beyond T*G of the Q tile are never written by TMA: zero them once so
+  // Rows beyond T*G of the Q buffers are never written by TMA: zero them once so
   // the unused accumulator rows stay finite.
-  if (threadIdx.x < BM && threadIdx.x >= p.rows) {
-    uint4 z = make_uint4(0, 0, 0, 0);
-    uint4* r0 = reinterpret_cast<uint4*>(smem + OFF_Q + threadIdx.x * 128);
-    uint4* r1 = reinterpret_cast<uint4*>(smem + OFF_Q + HALF_BYTES + threadIdx.x * 128);
+  if (threadIdx.x < 2 * BM && (threadIdx.x & 127) >= p.rows) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    const int r = threadIdx.x & 127;
+    uint8_t* q = smem + OFF_Q + (threadIdx.x >> 7) * TILE_BYTES;
+    uint4* r0 = reinterpret_cast<uint4*>(q + r * 128);
+    uint4* r1 = reinterpret_cast<uint4*>(q + HALF_BYTES + r * 128);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       r0[i] = z;
@@ -189,20 +226,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int it = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-        const int g = u[kUKvHead], q_begin = u[kUQBegin];
+        const int g = u[kUKvHead];
         const int kb0 = u[kUKbBegin], kb1 = u[kUKbEnd];
         const int lu = ui - u_begin;
-        if (lu > 0 && !wait_or_abort(bars.q_empty, (lu - 1) & 1, VLC_DEV_ERR_TIMEOUT + 1, abort_flag))
+        const int qb = lu & 1;
+        if (lu >= 2 &&
+            !wait_or_abort(bars.q_empty + qb, (uint32_t)((lu >> 1) - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 1, abort_flag))
           break;
-        mbar_expect_tx(bars.q_full, 2 * p.rows * 128);
-        tma_load_3d(smem + OFF_Q, &p.tm_q, bars.q_full, 0, g * p.group, q_begin);
-        tma_load_3d(smem + OFF_Q + HALF_BYTES, &p.tm_q, bars.q_full, 64, g * p.group, q_begin);
+        uint8_t* qdst = smem + OFF_Q + qb * TILE_BYTES;
+        mbar_expect_tx(bars.q_full + qb, 2 * p.rows * 128);
+        tma_load_3d(qdst, &p.tm_q, bars.q_full + qb, 0, g * p.group, u[kUQBeginA]);
+        tma_load_3d(qdst + HALF_BYTES, &p.tm_q, bars.q_full + qb, 64, g * p.group, u[kUQBeginA]);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -228,184 +268,181 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         if (!ok) break;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // Global tile sequence t over this CTA's units.  For tile t it issues, in order:
+    // S(t+1) = Q K(t+1)^T (lookahead, also across a unit boundary), then
+    // O += P(t) V(t) once the softmax has written P(t).
+    if (lane == 0 && u_begin < u_end) {
       const uint32_t q_addr = smem_u32(smem + OFF_Q);
       const uint32_t k_addr = smem_u32(smem + OFF_K);
       const uint32_t v_addr = smem_u32(smem + OFF_V);
-      const uint32_t p_addr = smem_u32(smem + OFF_P);
-      int it = 0;  // global K/V tile counter (== S buffer / P / O counters)
-      bool ok = true;
-      auto do_pv = [&](int t) -> bool {
+      const uint32_t o_tmem = tmem_base + TMEM_O;
+      // cursor of the lookahead tile
+      int ui = u_begin, j = 0, na = 0;
+      auto unit_na = [&](int uu) {
+        const int32_t* u = p.units + (int64_t)uu * kUnitInts;
+        return u[kUKbEnd] - u[kUKbBegin];
+      };
+      // Issue S(t) for the tile at cursor (ui, j); returns false on abort.
+      auto issue_s = [&](int t, int uu, int jj, int nn) -> bool {
+        const int lu = uu - u_begin;
+        if (jj == 0) {
+          if (!wait_or_abort(bars.q_full + (lu & 1), (uint32_t)(lu >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 6, abort_flag))
+            return false;
+        }
         const int s = t % STAGES;
-        if (!wait_or_abort(bars.p_full, (uint32_t)t & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) return false;
-        if (!wait_or_abort(bars.v_full + s, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag))
+        if (!wait_or_abort(bars.k_full + s, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 7, abort_flag))
           return false;
         tc_fence_after();
+        issue_qk(tmem_base + TMEM_S + (t & 1) * 128, q_addr + (lu & 1) * TILE_BYTES, k_addr + s * TILE_BYTES);
+        umma_commit(bars.s_full + (t & 1));
+        umma_commit(bars.k_empty + s);
+        if (jj == nn - 1) umma_commit(bars.q_empty + (lu & 1));
         return true;
       };
-      for (int ui = u_begin; ui < u_end && ok; ++ui) {
-        const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-        const int n = u[kUKbEnd] - u[kUKbBegin];
-        const int lu = ui - u_begin;
-        if (!wait_or_abort(bars.q_full, (uint32_t)lu & 1u, VLC_DEV_ERR_TIMEOUT + 6, abort_flag)) break;
-        tc_fence_after();
-        const int t_first = it;
-        for (int i = 0; i < n; ++i, ++it) {
-          const int s = it % STAGES;
-          if (!wait_or_abort(bars.k_full + s, (uint32_t)(it / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 7, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d_s = tmem_base + ((it & 1) ? TMEM_S1 : TMEM_S0);
-          const uint32_t kb_addr = k_addr + s * TILE_BYTES;
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k) {
-            const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-            umma_ss(d_s, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(kb_addr + off, 16, 1024),
-                    IDESC_QK, k > 0 ? 1u : 0u);
-          }
-          umma_commit(bars.s_full + (it & 1));
-          umma_commit(bars.k_empty + s);
-          if (i == n - 1) umma_commit(bars.q_empty);
-          if (i > 0) {
-            const int t = it - 1;
-            if (!do_pv(t)) {
-              ok = false;
-              break;
-            }
-            const uint32_t vb = v_addr + (t % STAGES) * TILE_BYTES;
-#pragma unroll
-            for (int k = 0; k < BN / 16; ++k) {
-              const uint32_t aoff = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-              umma_ss(tmem_base + TMEM_O, umma_desc_sw128(p_addr + aoff, 16, 1024),
-                      umma_desc_sw128(vb + k * 2048, HALF_BYTES, 1024), IDESC_PV,
-                      (t > t_first || k > 0) ? 1u : 0u);
-            }
-            umma_commit(bars.v_empty + (t % STAGES));
-            umma_commit(bars.o_done);
-          }
+      na = unit_na(ui);
+      bool ok = issue_s(0, ui, 0, na);
+      int t = 0;
+      while (ok) {
+        // cursor (ui, j) is tile t; find tile t+1
+        int un = ui, jn = j + 1, nn = na;
+        if (jn == na) {
+          un = ui + 1;
+          jn = 0;
+          nn = un < u_end ? unit_na(un) : 0;
         }
+        if (un < u_end) ok = issue_s(t + 1, un, jn, nn);
         if (!ok) break;
-        // PV of the unit's last tile.
-        const int t = it - 1;
-        if (!do_pv(t)) break;
-        const uint32_t vb = v_addr + (t % STAGES) * TILE_BYTES;
-#pragma unroll
-        for (int k = 0; k < BN / 16; ++k) {
-          const uint32_t aoff = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-          umma_ss(tmem_base + TMEM_O, umma_desc_sw128(p_addr + aoff, 16, 1024),
-                  umma_desc_sw128(vb + k * 2048, HALF_BYTES, 1024), IDESC_PV,
-                  (t > t_first || k > 0) ? 1u : 0u);
-        }
-        umma_commit(bars.v_empty + (t % STAGES));
+        // O += P(t) V(t)
+        const int s = t % STAGES;
+        if (!wait_or_abort(bars.p_full + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag) ||
+            !wait_or_abort(bars.v_full + s, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag))
+          break;
+        tc_fence_after();
+        issue_pv(o_tmem, tmem_base + TMEM_S + (t & 1) * 128, v_addr + s * TILE_BYTES, j > 0);
+        umma_commit(bars.v_empty + s);
         umma_commit(bars.o_done);
+        ++t;
+        ui = un;
+        j = jn;
+        na = nn;
+        if (ui >= u_end) break;
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroup
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    uint8_t* p_row0 = smem + OFF_P + row * 128;
-    const int sw = row & 7;
-    int it = 0;
+    // ------------------------------------------------------------ softmax (two column halves)
+    const int h = warp >> 2;            // 0: columns 0-63, 1: columns 64-127
+    const int row = threadIdx.x & 127;  // == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t o_addr = tmem_base + lane_off + TMEM_O + h * 64;
+    float* xmax = reinterpret_cast<float*>(smem + OFF_X);   // [parity][half][row]
+    float* xsum = reinterpret_cast<float*>(smem + OFF_L);   // [half][row]
+    int t = 0;  // global tile counter
     for (int ui = u_begin; ui < u_end; ++ui) {
       const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-      const int g = u[kUKvHead], q_begin = u[kUQBegin], q_count = u[kUQCount];
-      const int kpos0 = u[kUKpos0], kb0 = u[kUKbBegin], kb1 = u[kUKbEnd];
-      const int kv_len = u[kUKvLen], part = u[kUPart];
+      const int lu = ui - u_begin;
+      const int g = u[kUKvHead];
+      const int kb0 = u[kUKbBegin];
+      const int n = u[kUKbEnd] - kb0;
+      const int kv_len = u[kUKvLen];
+      const int q_begin = u[kUQBeginA], q_count = u[kUQCountA];
+      const int kpos0 = u[kUKpos0A];
+      const int part = u[kUPartA];
       const int tok = row / p.group;
       const bool row_valid = row < p.rows && tok < q_count;
       const int qpos = kpos0 + tok;
       float m_use = -INFINITY;
-      float l_sum = 0.f;
+      float l_part = 0.f;   // this half's share of the row sum
       bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        if (!wait_or_abort(bars.s_full + (it & 1), (uint32_t)(it >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
+      for (int j = 0; j < n; ++j, ++t) {
+        const uint32_t s_addr = tmem_base + lane_off + TMEM_S + (t & 1) * 128;
+        if (!wait_or_abort(bars.s_full + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 9, abort_flag)) {
           ok = false;
           break;
         }
         __syncwarp();
         tc_fence_after();
-        const uint32_t s_addr = tmem_base + lane_off + ((it & 1) ? TMEM_S1 : TMEM_S0);
-        uint32_t sr[4][32];
-        tmem_ld32(s_addr + 0, sr[0]);
-        tmem_ld32(s_addr + 32, sr[1]);
-        tmem_ld32(s_addr + 64, sr[2]);
-        tmem_ld32(s_addr + 96, sr[3]);
+        const int key0 = (kb0 + j) * BN;
+        uint32_t sr[64];
+        tmem_ld32(s_addr + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld32(s_addr + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
         tmem_wait_ld();
-        float* s = reinterpret_cast<float*>(&sr[0][0]);
-        const int key0 = kb * BN;
         if (key0 + BN - 1 > kpos0) {  // tile touches the causal diagonal
-          const int lim = qpos - key0;
+          const int lim = qpos - key0 - h * 64;
 #pragma unroll
-          for (int c = 0; c < BN; ++c)
-            if (c > lim) s[c] = -INFINITY;
+          for (int c = 0; c < 64; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
         }
-        float mx = s[0];
+        float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
+        float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
 #pragma unroll
-        for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
-        const float m_tile = mx * p.scale_log2;
-        // P smem buffer and O are free once PV of the previous tile finished.
-        if (kb > kb0) {
-          if (!wait_or_abort(bars.o_done, (uint32_t)(it - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 9, abort_flag)) {
+        for (int c = 4; c < 64; c += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[c]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[c + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(sr[c + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(sr[c + 3]));
+        }
+        // Exchange the half-row maxima (double-buffered by tile parity).  The barrier
+        // also orders this half's S loads before the other half overwrites S with P.
+        float* xm = xmax + (t & 1) * 2 * BM;
+        xm[h * BM + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        tc_fence_before();
+        mbar_arrive(bars.xchg + (t & 1));
+        if (!wait_or_abort(bars.xchg + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 13, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float m_tile = fmaxf(xm[row], xm[BM + row]) * p.scale_log2;
+        // Lazy rescaling: only move the reference max when it grows by > 2^8.
+        const bool need = m_tile > m_use + 8.0f;
+        if (__any_sync(0xffffffffu, need && j > 0)) {
+          // O must be stable: wait for the previous tile's P*V.
+          if (!wait_or_abort(bars.o_done, (uint32_t)(t - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 10, abort_flag)) {
             ok = false;
             break;
           }
+          __syncwarp();
           tc_fence_after();
-        }
-        // Lazy rescaling: only move the reference max when it grows by > 2^8.
-        const bool need = m_tile > m_use + 8.0f;
-        if (__any_sync(0xffffffffu, need && kb > kb0)) {
           const float m_new = need ? m_tile : m_use;
           const float f = (need && m_use != -INFINITY) ? fast_exp2(m_use - m_new) : 1.0f;
-          if (kb > kb0) {
-            const uint32_t o_addr = tmem_base + lane_off + TMEM_O;
+#pragma unroll 1
+          for (int cb = 0; cb < 2; ++cb) {
+            uint32_t orr[32];
+            tmem_ld32(o_addr + cb * 32, orr);
+            tmem_wait_ld();
 #pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-              uint32_t orr[32];
-              tmem_ld32(o_addr + cb * 32, orr);
-              tmem_wait_ld();
-#pragma unroll
-              for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * f);
-              tmem_st32(o_addr + cb * 32, orr);
-            }
-            tmem_wait_st();
+            for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * f);
+            tmem_st32(o_addr + cb * 32, orr);
           }
-          l_sum *= f;
+          l_part *= f;
           m_use = m_new;
         } else if (need) {
           m_use = m_tile;  // first tile of the unit
         }
         const float mref = (m_use == -INFINITY) ? 0.f : m_use;
-        // P = exp2(s * scale_log2 - mref) -> bf16, SW128 K-major layout.
+        // P = exp2(s * scale_log2 - mref) as bf16 pairs; pair c reuses register c.
+        float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
-          float e[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            e[j] = fast_exp2(fmaf(s[ch * 8 + j], p.scale_log2, -mref));
-            l_sum += e[j];
-          }
-          uint4 pk;
-          pk.x = pack_bf16x2(e[0], e[1]);
-          pk.y = pack_bf16x2(e[2], e[3]);
-          pk.z = pack_bf16x2(e[4], e[5]);
-          pk.w = pack_bf16x2(e[6], e[7]);
-          const int h = ch >> 3, cc = ch & 7;
-          *reinterpret_cast<uint4*>(p_row0 + h * HALF_BYTES + ((cc ^ sw) << 4)) = pk;
+        for (int c = 0; c < 32; ++c) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, -mref));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, -mref));
+          l0 += e0;
+          l1 += e1;
+          sr[c] = pack_bf16x2(e0, e1);
         }
+        l_part += l0 + l1;
+        tmem_st32(s_addr + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
         // Keys past the sequence end: zero their V rows so 0 * garbage stays 0.
-        if (key0 + BN > kv_len) {
-          const int st = it % STAGES;
-          if (!wait_or_abort(bars.v_full + st, (uint32_t)(it / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 10, abort_flag)) {
+        if (h == 0 && key0 + BN > kv_len) {
+          const int st = t % STAGES;
+          if (!wait_or_abort(bars.v_full + st, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) {
             ok = false;
             break;
           }
           if (key0 + row >= kv_len) {
-            uint4 z = make_uint4(0, 0, 0, 0);
+            const uint4 z = make_uint4(0, 0, 0, 0);
             uint4* v0 = reinterpret_cast<uint4*>(smem + OFF_V + st * TILE_BYTES + row * 128);
             uint4* v1 = reinterpret_cast<uint4*>(smem + OFF_V + st * TILE_BYTES + HALF_BYTES + row * 128);
 #pragma unroll
@@ -414,104 +451,122 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
               v1[i] = z;
             }
           }
+          fence_proxy_async_smem();
         }
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bars.p_full);
+        mbar_arrive(bars.p_full + (t & 1));
       }
       if (!ok) break;
       // ---------------------------------------------------------- epilogue
-      if (!wait_or_abort(bars.o_done, (uint32_t)(it - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) break;
+      xsum[h * BM + row] = l_part;
+      mbar_arrive(bars.xsum);
+      if (!wait_or_abort(bars.xsum, (uint32_t)lu & 1u, VLC_DEV_ERR_TIMEOUT + 14, abort_flag)) break;
+      const float l_sum = xsum[row] + xsum[BM + row];
+      if (!wait_or_abort(bars.o_done, (uint32_t)(t - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 12, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      const uint32_t o_addr = tmem_base + lane_off + TMEM_O;
+      const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
+      __nv_bfloat16* dst;
       if (part < 0) {
-        const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
         const int head = g * p.group + (row - tok * p.group);
-        __nv_bfloat16* dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * HD;
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          uint32_t orr[32];
-          tmem_ld32(o_addr + cb * 32, orr);
-          tmem_wait_ld();
-          if (row_valid) {
-#pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-              uint4 pk;
-              pk.x = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 0]) * inv, __uint_as_float(orr[c8 * 8 + 1]) * inv);
-              pk.y = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 2]) * inv, __uint_as_float(orr[c8 * 8 + 3]) * inv);
-              pk.z = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 4]) * inv, __uint_as_float(orr[c8 * 8 + 5]) * inv);
-              pk.w = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 6]) * inv, __uint_as_float(orr[c8 * 8 + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + cb * 32 + c8 * 8) = pk;
-            }
-          }
-        }
+        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * HD + h * 64;
       } else {
-        float* po = p.part_o + ((int64_t)part * BM + row) * HD;
+        // Split partial: O / l as bf16 (the merge re-weights by l and the max).
+        dst = p.part_o + ((int64_t)part * BM + row) * HD + h * 64;
+        if (h == 0) reinterpret_cast<float2*>(p.part_ml)[(int64_t)part * BM + row] = make_float2(m_use, l_sum);
+      }
+      const bool store = part < 0 ? row_valid : true;
+#pragma unroll 1
+      for (int cb = 0; cb < 2; ++cb) {
+        uint32_t orr[32];
+        tmem_ld32(o_addr + cb * 32, orr);
+        tmem_wait_ld();
+        if (store) {
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          uint32_t orr[32];
-          tmem_ld32(o_addr + cb * 32, orr);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            *reinterpret_cast<uint4*>(po + cb * 32 + c4 * 4) =
-                make_uint4(orr[c4 * 4 + 0], orr[c4 * 4 + 1], orr[c4 * 4 + 2], orr[c4 * 4 + 3]);
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 0]) * inv, __uint_as_float(orr[c8 * 8 + 1]) * inv);
+            pk.y = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 2]) * inv, __uint_as_float(orr[c8 * 8 + 3]) * inv);
+            pk.z = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 4]) * inv, __uint_as_float(orr[c8 * 8 + 5]) * inv);
+            pk.w = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 6]) * inv, __uint_as_float(orr[c8 * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + cb * 32 + c8 * 8) = pk;
           }
         }
-        float2* ml = reinterpret_cast<float2*>(p.part_ml) + (int64_t)part * BM + row;
-        *ml = make_float2(m_use, l_sum);
       }
       tc_fence_before();
     }
   }
 
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-// Merge split units: O = sum_p 2^(m_p - M) O_p / sum_p 2^(m_p - M) l_p.
-// One warp per tile row; lanes cover the 128 dims (4 each).
+// Merge split units.  Part p holds O_p / l_p (bf16), its max m_p and sum l_p:
+//   O = sum_p w_p (O_p / l_p) / sum_p w_p,   w_p = 2^(m_p - M) l_p.
+// One warp per tile row (8 rows per 256-thread block, every row of every merge in
+// flight at once); lane p reads part p's (m, l) so the weights take one round of
+// shuffles, and each lane accumulates 4 of the 128 dims over the parts with
+// independent loads.
+constexpr int kMergeRowsPerBlock = 8;
+
 __global__ void __launch_bounds__(256) prefill_merge_kernel(const int32_t* __restrict__ merges,
-                                                            const float* __restrict__ part_o,
+                                                            const __nv_bfloat16* __restrict__ part_o,
                                                             const float* __restrict__ part_ml,
-                                                            int group, int rows,
+                                                            int group, int rows, int blocks_per_merge,
                                                             __nv_bfloat16* __restrict__ out,
                                                             int64_t out_token_stride) {
-  const int32_t* m = merges + (int64_t)blockIdx.x * kMergeInts;
-  const int q_begin = m[kMQBegin], q_count = m[kMQCount], g = m[kMKvHead];
-  const int part0 = m[kMPartBegin], nparts = m[kMNumParts];
+  const int mi = blockIdx.x / blocks_per_merge;
+  const int row = (blockIdx.x - mi * blocks_per_merge) * kMergeRowsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  for (int row = blockIdx.y * 8 + (threadIdx.x >> 5); row < rows; row += gridDim.y * 8) {
-    const int tok = row / group;
-    if (tok >= q_count) continue;
-    float M = -INFINITY;
-    for (int i = 0; i < nparts; ++i) M = fmaxf(M, part_ml[((int64_t)(part0 + i) * BM + row) * 2]);
-    const float mref = (M == -INFINITY) ? 0.f : M;
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < nparts; ++i) {
-      const int64_t pr = (int64_t)(part0 + i) * BM + row;
-      const float mi = part_ml[pr * 2], li = part_ml[pr * 2 + 1];
-      const float w = (mi == -INFINITY) ? 0.f : exp2f(mi - mref);
-      L += w * li;
-      const float4 o = reinterpret_cast<const float4*>(part_o + pr * HD)[lane];
-      acc.x += w * o.x;
-      acc.y += w * o.y;
-      acc.z += w * o.z;
-      acc.w += w * o.w;
+  const int32_t* m = merges + (int64_t)mi * kMergeInts;
+  const int q_begin = __ldg(m + kMQBegin), q_count = __ldg(m + kMQCount), g = __ldg(m + kMKvHead);
+  const int part0 = __ldg(m + kMPartBegin), nparts = __ldg(m + kMNumParts);
+  if (row >= rows) return;
+  const int tok = row / group;
+  if (tok >= q_count) return;
+  const float2* ml = reinterpret_cast<const float2*>(part_ml);
+  // Pass 1: global max over the parts (lanes stride over parts).
+  float M = -INFINITY;
+  for (int i = lane; i < nparts; i += 32) M = fmaxf(M, __ldg(&ml[(int64_t)(part0 + i) * BM + row].x));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float mref = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int base = 0; base < nparts; base += 32) {
+    float w = 0.f;
+    if (base + lane < nparts) {
+      const float2 v = __ldg(&ml[(int64_t)(part0 + base + lane) * BM + row]);
+      w = (v.x == -INFINITY) ? 0.f : exp2f(v.x - mref) * v.y;  // weight of O_p/l_p is 2^(m_p-M) l_p
+      L += w;
     }
-    const float inv = L > 0.f ? 1.0f / L : 0.f;
-    const int head = g * group + (row - tok * group);
-    __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * HD + lane * 4;
-    uint2 pk;
-    pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-    pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(dst) = pk;
+    const int n = min(32, nparts - base);
+#pragma unroll 4
+    for (int i = 0; i < n; ++i) {
+      const float wi = __shfl_sync(0xffffffffu, w, i);
+      if (wi == 0.f) continue;  // empty or fully masked part (its O may be unwritten)
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(part_o + ((int64_t)(part0 + base + i) * BM + row) * HD) + lane);
+      const float2 o01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+      const float2 o23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+      acc.x += wi * o01.x;
+      acc.y += wi * o01.y;
+      acc.z += wi * o23.x;
+      acc.w += wi * o23.y;
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  const int head = g * group + (row - tok * group);
+  __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * HD + lane * 4;
+  uint2 pk;
+  pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(dst) = pk;
 }
 
 }  // namespace prefill
@@ -523,7 +578,7 @@ using namespace vlc::prefill;
 extern "C" int64_t vlc_prefill_workspace_size(const int32_t* plan_host) {
   if (!plan_host || plan_host[kPMagic] != kPlanMagic) return -1;
   const int64_t parts = plan_host[kPNumParts];
-  return parts * (int64_t)BM * (HD + 2) * (int64_t)sizeof(float);
+  return parts * (int64_t)BM * (HD * (int64_t)sizeof(__nv_bfloat16) + 2 * (int64_t)sizeof(float));
 }
 
 extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num_heads,
@@ -582,10 +637,9 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   prm.num_slots = num_slots;
   prm.out = (__nv_bfloat16*)out;
   prm.out_token_stride = out_token_stride;
-  float* ws = (float*)workspace;
   const int64_t parts = plan_host[kPNumParts];
-  prm.part_o = ws;
-  prm.part_ml = ws ? ws + parts * BM * HD : nullptr;
+  prm.part_ml = (float*)workspace;  // [parts][BM][2] fp32 first (8-byte aligned), then bf16 O
+  prm.part_o = workspace ? (__nv_bfloat16*)((float*)workspace + parts * BM * 2) : nullptr;
 
   static bool attr_set = false;
   if (!attr_set) {
@@ -600,9 +654,9 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   if (rc != VLC_OK) return rc;
   const int nmerge = plan_host[kPNumMerges];
   if (nmerge > 0) {
-    dim3 mg(nmerge, (rows + 7) / 8 < 4 ? (rows + 7) / 8 : 4);
-    prefill_merge_kernel<<<mg, 256, 0, st>>>(plan_dev + plan_host[kPOffMerges], prm.part_o, prm.part_ml,
-                                             group, rows, prm.out, out_token_stride);
+    const int bpm = (rows + kMergeRowsPerBlock - 1) / kMergeRowsPerBlock;
+    prefill_merge_kernel<<<nmerge * bpm, 32 * kMergeRowsPerBlock, 0, st>>>(
+        plan_dev + plan_host[kPOffMerges], prm.part_o, prm.part_ml, group, rows, bpm, prm.out, out_token_stride);
     rc = launch_status();
   }
   return rc;
