@@ -49,9 +49,14 @@ constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
 constexpr int OFF_X = OFF_V + STAGES * TILE_BYTES;     // row-max exchange [2 parity][2 halves][128]
 constexpr int OFF_L = OFF_X + 2 * 2 * BM * 4;          // row-sum exchange [2 halves][128]
 constexpr int OFF_BAR = OFF_L + 2 * BM * 4;
-// barriers: q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done,
-//           xchg[2] (half-row maxima, by tile parity), xsum (row sums, per unit)
-constexpr int NUM_BARS = 4 + 4 * STAGES + 5 + 3;
+// barriers: q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2],
+//           o_done[2] (P*V of tile t completes o_done[t % 2]), xchg[2] (half-row maxima, by tile
+//           parity), xsum (row sums, per unit).
+// A parity wait is only sound if the barrier is at most one phase behind the completion
+// waited for.  For o_done that holds per buffer: S(t) is issued only after P(t-2)*V, so
+// a thread that has seen S(t) knows P*V of tile t-2 is complete.  (A single o_done
+// barrier could be two phases behind and accept an older completion.)
+constexpr int NUM_BARS = 4 + 4 * STAGES + 6 + 3;
 constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 
@@ -92,7 +97,7 @@ struct Bars {
   uint64_t* v_empty;
   uint64_t* s_full;   // [2]
   uint64_t* p_full;   // [2]
-  uint64_t* o_done;
+  uint64_t* o_done;   // [2]
   uint64_t* xchg;     // [2]
   uint64_t* xsum;
 };
@@ -109,8 +114,8 @@ __device__ __forceinline__ Bars make_bars(uint8_t* smem) {
   r.s_full = b + 4 + 4 * STAGES;
   r.p_full = b + 6 + 4 * STAGES;
   r.o_done = b + 8 + 4 * STAGES;
-  r.xchg = b + 9 + 4 * STAGES;
-  r.xsum = b + 11 + 4 * STAGES;
+  r.xchg = b + 10 + 4 * STAGES;
+  r.xsum = b + 12 + 4 * STAGES;
   return r;
 }
 
@@ -195,7 +200,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       mbar_init(bars.v_full + s, 1);
       mbar_init(bars.v_empty + s, 1);
     }
-    mbar_init(bars.o_done, 1);
+    mbar_init(bars.o_done + 0, 1);
+    mbar_init(bars.o_done + 1, 1);
     mbar_init(bars.xchg + 0, kSoftmaxThreads);
     mbar_init(bars.xchg + 1, kSoftmaxThreads);
     mbar_init(bars.xsum, kSoftmaxThreads);
@@ -322,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         tc_fence_after();
         issue_pv(o_tmem, tmem_base + TMEM_S + (t & 1) * 128, v_addr + s * TILE_BYTES, j > 0);
         umma_commit(bars.v_empty + s);
-        umma_commit(bars.o_done);
+        umma_commit(bars.o_done + (t & 1));
         ++t;
         ui = un;
         j = jn;
@@ -399,7 +405,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         const bool need = m_tile > m_use + 8.0f;
         if (__any_sync(0xffffffffu, need && j > 0)) {
           // O must be stable: wait for the previous tile's P*V.
-          if (!wait_or_abort(bars.o_done, (uint32_t)(t - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 10, abort_flag)) {
+          if (!wait_or_abort(bars.o_done + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 10,
+                             abort_flag)) {
             ok = false;
             break;
           }
@@ -463,7 +470,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       mbar_arrive(bars.xsum);
       if (!wait_or_abort(bars.xsum, (uint32_t)lu & 1u, VLC_DEV_ERR_TIMEOUT + 14, abort_flag)) break;
       const float l_sum = xsum[row] + xsum[BM + row];
-      if (!wait_or_abort(bars.o_done, (uint32_t)(t - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 12, abort_flag)) break;
+      if (!wait_or_abort(bars.o_done + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 12,
+                         abort_flag))
+        break;
       __syncwarp();
       tc_fence_after();
       const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
