@@ -118,6 +118,17 @@ def _coverage(cu_q, cu_k, H, Hk, num_sms):
     assert parts_seen == set(range(nparts))
     for m in merges:
         assert m[4] >= 2
+        assert m[5] in (1, 2, 4) and m[6] == m[1] * G
+    # merge launch: (merge << 8 | first row) per 8-warp block covers every valid row once
+    h = plan.host
+    nblk, off = int(h[16]), int(h[17])
+    seen = {}
+    for e in h[off:off + nblk]:
+        mi, r0 = int(e) >> 8, int(e) & 255
+        rpb = 8 * int(merges[mi][5])
+        for r in range(r0, min(r0 + rpb, int(merges[mi][6]))):
+            seen[(mi, r)] = seen.get((mi, r), 0) + 1
+    assert seen == {(mi, r): 1 for mi in range(len(merges)) for r in range(int(merges[mi][6]))}
     return plan
 
 

@@ -4,10 +4,11 @@
 // runner produces (nanovllm/engine/model_runner.py:194-320 prepare_prefill:
 // cu_seqlens_q, cu_seqlens_k with bottom-right causal alignment) and bin-packs
 // them onto a persistent grid of one CTA per SM (longest-processing-time first).
-// A unit is one query tile over one range of 128-key blocks.  Tiles whose key
-// range is long (text after the image sees the whole image) are split into
-// several units so the per-CTA work is balanced; the partial results are merged
-// by a second small kernel.
+// A unit is a pair of query tiles of one (sequence, KV head) sharing one range
+// of 128-key blocks (or a single tile).  Units whose key range is long (text
+// after the image sees the whole image) are split into several units so the
+// per-CTA work is balanced; the partial results are merged by a second small
+// kernel.
 //
 // Pure host code (the only CUDA query is the SM count when num_sms == 0, which
 // falls back to 148 without a device): usable without a GPU.
@@ -88,7 +89,7 @@ extern "C" int64_t vlc_prefill_plan_capacity(const int32_t* cu_q, const int32_t*
   for (const Tile& t : tiles) total_kb += t.n_kb;
   const int64_t max_units = (int64_t)tiles.size() + total_kb;
   return vlc::kPlanHeaderInts + (num_sms + 1) + max_units * vlc::kUnitInts +
-         (int64_t)tiles.size() * vlc::kMergeInts;
+         (int64_t)tiles.size() * (vlc::kMergeInts + kTileRows);
 }
 
 extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_heads,
@@ -104,15 +105,46 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   std::vector<Tile> tiles;
   build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, tiles);
 
-  // Time model (in key-block iterations of one tile): each unit pays a fixed
-  // start/epilogue cost, each split part a partial write and its share of the merge.
-  const double kUnitOverhead = 1.5, kPartOverhead = 0.5;
+  // Pair the tiles of each (sequence, KV head) from the end: (last, second last),
+  // ...; with an odd count the first (cheapest) tile stays alone.  The later tile
+  // of a pair is tile A (it sees every key block tile B sees, and maybe one more).
+  struct Pair {
+    int a, b;  // tile indices, b = -1 for a single tile
+  };
+  std::vector<Pair> pairs;
+  for (size_t i = 0; i < tiles.size();) {
+    size_t e = i;
+    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head) ++e;
+    int last = (int)e - 1;
+    while (last >= (int)i) {
+      if (last - 1 >= (int)i) {
+        pairs.push_back(Pair{last, last - 1});
+        last -= 2;
+      } else {
+        pairs.push_back(Pair{last, -1});
+        last -= 1;
+      }
+    }
+    i = e;
+  }
+
+  // Time model, in key-block steps: a step of a paired unit costs a little more
+  // than a single-tile step (the two tiles' softmaxes share the SM), each unit
+  // pays a fixed start/epilogue cost, each split part a partial write and its
+  // share of the merge.
+  const double kUnitOverhead = 2.0, kPartOverhead = 0.3, kPairStep = 0.33;
+  auto pair_cost = [&](const Pair& pr, int kb0, int kb1) {
+    const int nb = pr.b >= 0 ? std::max(0, std::min(kb1, tiles[pr.b].n_kb) - kb0) : 0;
+    return (kb1 - kb0) + kPairStep * nb + kUnitOverhead;
+  };
   double total_time = 0.0;
-  for (const Tile& t : tiles) total_time += t.n_kb + kUnitOverhead;
+  for (const Pair& pr : pairs) total_time += pair_cost(pr, 0, tiles[pr.a].n_kb);
   const double avg = total_time / std::max(1, num_sms);
-  // Split only tiles well above the per-SM average, into parts of about the average.
-  const double split_above = std::max(4.0, 1.5 * avg);
-  const double target = std::max(3.0, avg);
+  // Split units well above the per-SM average into parts of about the average:
+  // every part writes a 32 KB partial per tile that the merge reads back, so the
+  // split count trades balance against merge traffic.
+  const double split_above = std::max(3.0, 1.5 * avg);
+  const double target = std::max(2.0, 1.2 * avg / (1.0 + kPairStep));
   std::vector<UnitRec> units;
   std::vector<std::array<int32_t, kMergeInts>> merges;
   int num_parts = 0;
@@ -123,21 +155,37 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
     m[kMKvHead] = t.kv_head;
     m[kMPartBegin] = part0;
     m[kMNumParts] = np;
+    // A warp is 4 groups of 8 lanes; few parts: one row per group, many parts:
+    // the groups of a warp split one row's parts.
+    m[kMRowsPerWarp] = np <= 4 ? 4 : np <= 8 ? 2 : 1;
+    m[kMRows] = t.q_count * G;
     merges.push_back(m);
   };
-  for (const Tile& ta : tiles) {
-    int np = ta.n_kb + kUnitOverhead > split_above ? (int)std::ceil(ta.n_kb / target) : 1;
-    np = std::max(1, std::min(np, ta.n_kb));
-    const int part0 = np > 1 ? num_parts : -1;
+  for (const Pair& pr : pairs) {
+    const Tile& ta = tiles[pr.a];
+    const int n = ta.n_kb;
+    int np = pair_cost(pr, 0, n) > split_above ? (int)std::ceil(n / target) : 1;
+    np = std::max(1, std::min(np, n));
+    std::vector<int> cuts(np + 1);
+    for (int i = 0; i <= np; ++i) cuts[i] = (int)((int64_t)n * i / np);
+    // Parts of tile A: all np; parts of tile B: those that start before its end.
+    const int nb_full = pr.b >= 0 ? tiles[pr.b].n_kb : 0;
+    int np_b = 0;
+    while (np_b < np && cuts[np_b] < nb_full) ++np_b;
+    const int part_a = np > 1 ? num_parts : -1;
     if (np > 1) {
-      add_merge(ta, part0, np);
+      add_merge(ta, part_a, np);
       num_parts += np;
+    }
+    const int part_b = np_b > 1 ? num_parts : -1;
+    if (np_b > 1) {
+      add_merge(tiles[pr.b], part_b, np_b);
+      num_parts += np_b;
     }
     for (int i = 0; i < np; ++i) {
       UnitRec u{};
       for (int k = 0; k < kUnitInts; ++k) u.f[k] = 0;
-      const int kb0 = (int)((int64_t)ta.n_kb * i / np);
-      const int kb1 = (int)((int64_t)ta.n_kb * (i + 1) / np);
+      const int kb0 = cuts[i], kb1 = cuts[i + 1];
       u.f[kUSeq] = ta.seq;
       u.f[kUKvHead] = ta.kv_head;
       u.f[kUKbBegin] = kb0;
@@ -147,11 +195,17 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
       u.f[kUQBeginA] = ta.q_begin;
       u.f[kUQCountA] = ta.q_count;
       u.f[kUKpos0A] = ta.kpos0;
-      u.f[kUPartA] = np > 1 ? part0 + i : -1;
-      u.f[kUQCountB] = 0;  // single-tile units (tile B fields unused)
+      u.f[kUPartA] = np > 1 ? part_a + i : -1;
       u.f[kUPartB] = -1;
-      u.f[kUKbEndB] = kb0;
-      u.cost = (kb1 - kb0) + kUnitOverhead + (np > 1 ? kPartOverhead : 0.0);
+      if (i < np_b) {
+        const Tile& tb = tiles[pr.b];
+        u.f[kUQBeginB] = tb.q_begin;
+        u.f[kUQCountB] = tb.q_count;
+        u.f[kUKpos0B] = tb.kpos0;
+        u.f[kUPartB] = np_b > 1 ? part_b + i : -1;
+        u.f[kUKbEndB] = std::min(kb1, nb_full);
+      }
+      u.cost = pair_cost(i < np_b ? pr : Pair{pr.a, -1}, kb0, kb1) + (np > 1 ? kPartOverhead : 0.0);
       u.f[kUCost] = (int32_t)(u.cost * 16);
       units.push_back(u);
     }
@@ -179,7 +233,14 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   const int64_t off_cta = kPlanHeaderInts;
   const int64_t off_units = off_cta + grid + 1;
   const int64_t off_merges = off_units + (int64_t)num_units * kUnitInts;
-  const int64_t total = off_merges + (int64_t)merges.size() * kMergeInts;
+  // Merge launch: 8 warps per block, kMRowsPerWarp rows per warp.
+  std::vector<int32_t> merge_blocks;
+  for (size_t i = 0; i < merges.size(); ++i) {
+    const int rpb = 8 * merges[i][kMRowsPerWarp];
+    for (int r0 = 0; r0 < merges[i][kMRows]; r0 += rpb) merge_blocks.push_back((int32_t)((i << 8) | r0));
+  }
+  const int64_t off_mblocks = off_merges + (int64_t)merges.size() * kMergeInts;
+  const int64_t total = off_mblocks + (int64_t)merge_blocks.size();
   if (total > plan_capacity) return VLC_ERR_PLAN;
 
   int32_t* h = plan_out;
@@ -200,6 +261,8 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   h[kPOffUnits] = (int32_t)off_units;
   h[kPOffMerges] = (int32_t)off_merges;
   h[kPTotalLen] = (int32_t)total;
+  h[kPMergeBlocks] = (int32_t)merge_blocks.size();
+  h[kPOffMergeBlocks] = (int32_t)off_mblocks;
   int32_t* cta = h + off_cta;
   int32_t* up = h + off_units;
   int pos = 0;
@@ -214,6 +277,7 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   int32_t* mp = h + off_merges;
   for (size_t i = 0; i < merges.size(); ++i)
     for (int k = 0; k < kMergeInts; ++k) mp[i * kMergeInts + k] = merges[i][k];
+  for (size_t i = 0; i < merge_blocks.size(); ++i) h[off_mblocks + i] = merge_blocks[i];
   *plan_len = total;
   return VLC_OK;
 }

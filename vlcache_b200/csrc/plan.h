@@ -8,8 +8,8 @@
 namespace vlc {
 
 constexpr int32_t kPlanMagic = 0x564C4350;  // 'VLCP'
-constexpr int32_t kPlanVersion = 3;
-constexpr int kPlanHeaderInts = 16;
+constexpr int32_t kPlanVersion = 4;
+constexpr int kPlanHeaderInts = 20;
 
 // header fields
 enum : int {
@@ -29,11 +29,15 @@ enum : int {
   kPOffUnits = 13,     // int32[num_units][kUnitInts]
   kPOffMerges = 14,    // int32[num_merges][kMergeInts]
   kPTotalLen = 15,
+  kPMergeBlocks = 16,     // blocks of the merge launch
+  kPOffMergeBlocks = 17,  // int32[merge_blocks]: (merge index << 8) | first row of the block
 };
 
-// A unit is one query tile (fields "A") of one (sequence, KV head) over one range
-// of 128-key blocks.  The "B" fields are reserved for a second tile sharing the
-// key range; the current kernel plans single-tile units (kUQCountB == 0).
+// A unit is one or two query tiles of one (sequence, KV head) over one range of
+// 128-key blocks; both tiles read the same K/V blocks.  Tile A holds the later
+// tokens and covers blocks [kb_begin, kb_end) (at least one); tile B, when
+// present (kUQCountB > 0), holds earlier tokens of the same sequence and covers
+// [kb_begin, kb_end_b) with kb_begin < kb_end_b <= kb_end.
 constexpr int kUnitInts = 16;
 enum : int {
   kUSeq = 0,       // row of block_tables
@@ -51,7 +55,7 @@ enum : int {
   kUQCountB = 12,
   kUKpos0B = 13,
   kUPartB = 14,
-  kUKbEndB = 15,   // one past tile B's last block (kb_begin .. kb_end_b may be empty)
+  kUKbEndB = 15,   // one past tile B's last block
 };
 
 // merge fields (one record per split query tile)
@@ -62,6 +66,8 @@ enum : int {
   kMKvHead = 2,
   kMPartBegin = 3,
   kMNumParts = 4,
+  kMRowsPerWarp = 5,  // rows one warp merges (4, 2 or 1: its 4 lane groups split a row's parts)
+  kMRows = 6,         // rows to merge (valid tokens x G)
 };
 
 }  // namespace vlc

@@ -7,24 +7,31 @@
 // Work decomposition (host planner, plan.cpp): a *tile* is T consecutive
 // query tokens of one sequence x the G query heads of one KV head, packed into
 // the 128 rows of a UMMA M=128 tile (row = token*G + head: GQA packing, so one
-// K/V tile feeds G heads).  A *unit* is a tile over a range of 128-key blocks;
-// long ranges are split into several units whose partial results are merged by
+// K/V tile feeds G heads).  A *unit* is a pair of tiles of the same (sequence,
+// KV head) -- A holds the later tokens, B the earlier ones -- over one range of
+// 128-key blocks: every K/V block loaded feeds 256 query rows.  Long ranges are
+// split into several units whose partial results are merged by
 // prefill_merge_kernel.  Units are bin-packed onto a persistent grid of one CTA
 // per SM.
 //
-// CTA roles (320 threads):
-//   warps 0-3  softmax, columns 0-63 of every S row   (thread i: row i = TMEM lane i)
-//   warps 4-7  softmax, columns 64-127 of every S row
-//   warp  8    TMA producer: Q tiles (double-buffered), K/V tiles (2-stage ring)
+// CTA roles (352 threads):
+//   warps 0-3  softmax of tile A (thread i: row i = TMEM lane i, all 128 keys)
+//   warps 4-7  softmax of tile B
+//   warp  8    TMA producer of K/V blocks (2-stage ring)
 //   warp  9    TMEM allocator + single-thread tcgen05.mma issuer
-// TMEM (512 columns): S0 | S1 | O (128 fp32 columns each).  S is double
-// buffered: Q*K^T of key tile j+1 runs while the softmax works on tile j.  Each
-// softmax thread handles half a row (64 values): the two halves exchange their
-// maxima through shared memory once per tile, then write P (bf16 pairs) back
-// over their half of the S buffer, where the next MMA reads it as the A operand
-// of O += P V (V is an MN-major smem operand).  Online softmax in the log2
-// domain with lazy rescaling: the running max moves (and O is rescaled) only
-// when it grows by more than 2^8.
+//   warp 10    TMA producer of Q tiles (2-slot ring: a tile's slot reloads for
+//              the next unit once its last Q K^T has run)
+// TMEM (512 columns): S_A | S_B | O_A | O_B, 128 fp32 columns each.  For each
+// key block j the issuer runs, per tile X in (A, B):  O_X += P_X(j) V(j) as soon
+// as the softmax of X has written P_X(j), then S_X = Q_X K(j+1)^T.  The two
+// tiles interleave on the tensor pipe: while one tile's softmax works, the
+// other tile's P*V and Q*K^T execute.  P (bf16 pairs) overwrites the first 64
+// columns of S_X and is read from TMEM as the A operand of O += P V (V is an
+// MN-major smem operand).  Online softmax in the log2 domain with lazy
+// rescaling: the running max moves (and O is rescaled) only when it grows by
+// more than 2^8.  The tensor pipe executes one thread's MMAs in issue order, so
+// when S_X(j) is complete so is P_X(j-1) V(j-1): a softmax thread that has seen
+// S_X(j) may rescale O_X without further waiting.
 #include <algorithm>
 #include <cmath>
 
@@ -35,39 +42,43 @@
 namespace vlc {
 namespace prefill {
 
-constexpr int BM = 128;   // tile rows (tokens * group)
-constexpr int BN = 128;   // keys per K/V tile
-constexpr int HD = 128;   // head dim
-constexpr int STAGES = 2; // K/V ring depth
-constexpr int NUM_THREADS = 320;
-constexpr int HALF_BYTES = BM * 128;          // 128 rows x 128 B (64 bf16)
-constexpr int TILE_BYTES = 2 * HALF_BYTES;    // 32 KB: full 128 x 128 bf16 tile
+constexpr int BM = 128;    // tile rows (tokens * group)
+constexpr int BN = 128;    // keys per K/V block
+constexpr int HD = 128;    // head dim
+constexpr int STAGES = 2;  // K/V ring depth
+constexpr int QSLOTS = 2;  // Q ring depth (a unit holds up to two)
+constexpr int NUM_THREADS = 352;
+constexpr int HALF_BYTES = BM * 128;        // 128 rows x 128 B (64 bf16)
+constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 32 KB: full 128 x 128 bf16 tile
 
-constexpr int OFF_Q = 0;                               // 2 buffers
-constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + QSLOTS * TILE_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr int OFF_X = OFF_V + STAGES * TILE_BYTES;     // row-max exchange [2 parity][2 halves][128]
-constexpr int OFF_L = OFF_X + 2 * 2 * BM * 4;          // row-sum exchange [2 halves][128]
-constexpr int OFF_BAR = OFF_L + 2 * BM * 4;
-// barriers: q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2],
-//           o_done[2] (P*V of tile t completes o_done[t % 2]), xchg[2] (half-row maxima, by tile
-//           parity), xsum (row sums, per unit).
-// A parity wait is only sound if the barrier is at most one phase behind the completion
-// waited for.  For o_done that holds per buffer: S(t) is issued only after P(t-2)*V, so
-// a thread that has seen S(t) knows P*V of tile t-2 is complete.  (A single o_done
-// barrier could be two phases behind and accept an older completion.)
-constexpr int NUM_BARS = 4 + 4 * STAGES + 6 + 3;
+constexpr int OFF_STG = OFF_V + STAGES * TILE_BYTES;  // epilogue staging: 64 output columns per tile
+constexpr int STG_TILE = HALF_BYTES;                   // 128 rows x 128 B, 128-byte swizzle
+constexpr int OFF_BAR = OFF_STG + 2 * STG_TILE;
+// barriers: q_full[3], q_empty[3], k_full[S], k_empty[S], v_full[S], v_empty[S],
+//           s_full[2], p_lo[2], p_hi[2], o_done[2] (index = tile: 0 A, 1 B).  p_lo: P of
+//           keys 0-63 written, p_hi: P of keys 64-127 written.
+// Every parity wait below is on a barrier that is at most one phase behind the
+// completion it waits for, and never ahead of it: each producer of a completion
+// first waits for the consumer of the previous one.
+constexpr int NUM_BARS = 2 * QSLOTS + 4 * STAGES + 8;
 constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S = 0;     // S buffer b at TMEM_S + 128 b
-constexpr uint32_t TMEM_O = 256;
+constexpr uint32_t TMEM_S = 0;    // S of tile x at TMEM_S + 128 x
+constexpr uint32_t TMEM_O = 256;  // O of tile x at TMEM_O + 128 x
 
 constexpr uint32_t IDESC_QK = umma_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, 128, false, true);
 
-constexpr int kSoftmaxThreads = 256;
+constexpr int kTileThreads = 128;  // softmax threads per tile
+// Of every 4 key pairs of P, how many take exp2 on the FMA pipe (exp2_fma) instead
+// of the special-function unit; the rest use ex2.approx.
+constexpr int kFmaExpPairsOf4 = 0;
 
 struct Params {
   CUtensorMap tm_q;   // dims {HD, num_heads, total_q}, box {64, G, T}
@@ -82,40 +93,42 @@ struct Params {
   int rows;            // T * G (<= 128)
   float scale_log2;    // softmax_scale * log2(e)
   int64_t num_slots;
+  CUtensorMap tm_o;   // out:    dims {HD, num_heads, total_q}, box {64, G, T}
+  CUtensorMap tm_p;   // part_o: dims {HD, num_parts * BM},   box {64, BM}
+  int tokens_per_tile;  // T
   __nv_bfloat16* out;
   int64_t out_token_stride;
+  int out_store32;        // out rows are 32-byte aligned: 256-bit stores
   __nv_bfloat16* part_o;  // [num_parts][BM][HD] partial O / l (bf16)
   float* part_ml;         // [num_parts][BM][2]  (max in log2 domain, sum)
 };
 
 struct Bars {
-  uint64_t* q_full;   // [2]
-  uint64_t* q_empty;  // [2]
+  uint64_t* q_full;   // [QSLOTS]
+  uint64_t* q_empty;  // [QSLOTS]
   uint64_t* k_full;
   uint64_t* k_empty;
   uint64_t* v_full;
   uint64_t* v_empty;
   uint64_t* s_full;   // [2]
-  uint64_t* p_full;   // [2]
+  uint64_t* p_lo;     // [2]
+  uint64_t* p_hi;     // [2]
   uint64_t* o_done;   // [2]
-  uint64_t* xchg;     // [2]
-  uint64_t* xsum;
 };
 
 __device__ __forceinline__ Bars make_bars(uint8_t* smem) {
   uint64_t* b = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   Bars r;
   r.q_full = b;
-  r.q_empty = b + 2;
-  r.k_full = b + 4;
-  r.k_empty = b + 4 + STAGES;
-  r.v_full = b + 4 + 2 * STAGES;
-  r.v_empty = b + 4 + 3 * STAGES;
-  r.s_full = b + 4 + 4 * STAGES;
-  r.p_full = b + 6 + 4 * STAGES;
-  r.o_done = b + 8 + 4 * STAGES;
-  r.xchg = b + 10 + 4 * STAGES;
-  r.xsum = b + 12 + 4 * STAGES;
+  r.q_empty = b + QSLOTS;
+  r.k_full = b + 2 * QSLOTS;
+  r.k_empty = r.k_full + STAGES;
+  r.v_full = r.k_full + 2 * STAGES;
+  r.v_empty = r.k_full + 3 * STAGES;
+  r.s_full = r.k_full + 4 * STAGES;
+  r.p_lo = r.s_full + 2;
+  r.p_hi = r.s_full + 4;
+  r.o_done = r.s_full + 6;
   return r;
 }
 
@@ -132,6 +145,18 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
       return false;
     }
   }
+}
+
+// Unit fields the roles need.
+struct UnitView {
+  int n_a, n_b;  // key blocks of tile A (the unit's length) and of tile B (0: no tile B)
+};
+
+__device__ __forceinline__ UnitView unit_view(const int32_t* u) {
+  UnitView v;
+  v.n_a = u[kUKbEnd] - u[kUKbBegin];
+  v.n_b = u[kUQCountB] > 0 ? u[kUKbEndB] - u[kUKbBegin] : 0;
+  return v;
 }
 
 // Row (slot) of the first key of 128-key block `kb` of a unit.  Paged mode
@@ -153,20 +178,27 @@ __device__ __forceinline__ int key_block_slot(const Params& p, const int32_t* u,
   return (int)slot;
 }
 
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+// Descriptor low words: q_lo / k_lo / v_lo address the tile's first byte; the K
+// steps of 16 add compile-time offsets (K-major: +32 B per step within a 64-column
+// half, +16 KB to the second half; MN-major V: +2 KB per 16 keys).
+constexpr uint32_t DESC_HI = umma_desc_sw128_hi(1024);
+
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
 #pragma unroll
   for (int k = 0; k < HD / 16; ++k) {
-    const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-    umma_ss(d_tmem, umma_desc_sw128(q_addr + off, 16, 1024), umma_desc_sw128(k_addr + off, 16, 1024), IDESC_QK,
-            k > 0 ? 1u : 0u);
+    const uint32_t off = (uint32_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
+    umma_ss_w(d_tmem, q_lo + off, DESC_HI, k_lo + off, DESC_HI, IDESC_QK, k > 0 ? 1u : 0u);
   }
 }
 
-__device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, bool accumulate) {
+// O += P V over keys [64 half, 64 half + 64) of the block.
+__device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_lo, int half,
+                                              bool accumulate) {
 #pragma unroll
-  for (int k = 0; k < BN / 16; ++k) {
-    umma_ts(o_tmem, p_tmem + k * 8, umma_desc_sw128(v_addr + k * 2048, HALF_BYTES, 1024), IDESC_PV,
-            (accumulate || k > 0) ? 1u : 0u);
+  for (int k = 0; k < 4; ++k) {
+    const int kk = half * 4 + k;
+    umma_ts_w(o_tmem, p_tmem + kk * 8, v_lo + (uint32_t)((kk * 2048) >> 4), DESC_HI, IDESC_PV,
+              (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
@@ -188,11 +220,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < QSLOTS; ++b) {
       mbar_init(bars.q_full + b, 1);
       mbar_init(bars.q_empty + b, 1);
-      mbar_init(bars.s_full + b, 1);
-      mbar_init(bars.p_full + b, kSoftmaxThreads);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bars.k_full + s, 1);
@@ -200,30 +230,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       mbar_init(bars.v_full + s, 1);
       mbar_init(bars.v_empty + s, 1);
     }
-    mbar_init(bars.o_done + 0, 1);
-    mbar_init(bars.o_done + 1, 1);
-    mbar_init(bars.xchg + 0, kSoftmaxThreads);
-    mbar_init(bars.xchg + 1, kSoftmaxThreads);
-    mbar_init(bars.xsum, kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bars.s_full + x, 1);
+      mbar_init(bars.p_lo + x, kTileThreads);
+      mbar_init(bars.p_hi + x, kTileThreads);
+      mbar_init(bars.o_done + x, 1);
+    }
     fence_mbar_init();
   }
   if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
   }
-  // Rows beyond T*G of the Q buffers are never written by TMA: zero them once so
+  if (warp == 10 && lane == 0) tma_prefetch_desc(&p.tm_q);
+  // Rows beyond T*G of the Q slots are never written by TMA: zero them once so
   // the unused accumulator rows stay finite.
-  if (threadIdx.x < 2 * BM && (threadIdx.x & 127) >= p.rows) {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    const int r = threadIdx.x & 127;
-    uint8_t* q = smem + OFF_Q + (threadIdx.x >> 7) * TILE_BYTES;
-    uint4* r0 = reinterpret_cast<uint4*>(q + r * 128);
-    uint4* r1 = reinterpret_cast<uint4*>(q + HALF_BYTES + r * 128);
+  for (int i = threadIdx.x; i < QSLOTS * BM; i += NUM_THREADS) {
+    const int r = i & 127;
+    if (r >= p.rows) {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      uint8_t* q = smem + OFF_Q + (i >> 7) * TILE_BYTES;
+      uint4* r0 = reinterpret_cast<uint4*>(q + r * 128);
+      uint4* r1 = reinterpret_cast<uint4*>(q + HALF_BYTES + r * 128);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      r0[i] = z;
-      r1[i] = z;
+      for (int k = 0; k < 8; ++k) {
+        r0[k] = z;
+        r1[k] = z;
+      }
     }
   }
   fence_proxy_async_smem();
@@ -232,23 +265,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == 10) {
+    // ------------------------------------------------------------ Q producer
+    if (lane == 0) {
+      int load = 0;
+      for (int ui = u_begin; ui < u_end; ++ui) {
+        const int32_t* u = p.units + (int64_t)ui * kUnitInts;
+        const int g = u[kUKvHead];
+        const int ntile = u[kUQCountB] > 0 ? 2 : 1;
+        bool ok = true;
+        for (int x = 0; x < ntile; ++x, ++load) {
+          const int slot = load % QSLOTS;
+          if (load >= QSLOTS && !wait_or_abort(bars.q_empty + slot, (uint32_t)((load / QSLOTS) & 1) ^ 1u,
+                                               VLC_DEV_ERR_TIMEOUT + 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int q_begin = u[x == 0 ? kUQBeginA : kUQBeginB];
+          uint8_t* qdst = smem + OFF_Q + slot * TILE_BYTES;
+          mbar_expect_tx(bars.q_full + slot, 2 * p.rows * 128);
+          tma_load_3d(qdst, &p.tm_q, bars.q_full + slot, 0, g * p.group, q_begin);
+          tma_load_3d(qdst + HALF_BYTES, &p.tm_q, bars.q_full + slot, 64, g * p.group, q_begin);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ K/V producer
     if (lane == 0) {
       int it = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         const int32_t* u = p.units + (int64_t)ui * kUnitInts;
         const int g = u[kUKvHead];
         const int kb0 = u[kUKbBegin], kb1 = u[kUKbEnd];
-        const int lu = ui - u_begin;
-        const int qb = lu & 1;
-        if (lu >= 2 &&
-            !wait_or_abort(bars.q_empty + qb, (uint32_t)((lu >> 1) - 1) & 1u, VLC_DEV_ERR_TIMEOUT + 1, abort_flag))
-          break;
-        uint8_t* qdst = smem + OFF_Q + qb * TILE_BYTES;
-        mbar_expect_tx(bars.q_full + qb, 2 * p.rows * 128);
-        tma_load_3d(qdst, &p.tm_q, bars.q_full + qb, 0, g * p.group, u[kUQBeginA]);
-        tma_load_3d(qdst + HALF_BYTES, &p.tm_q, bars.q_full + qb, 64, g * p.group, u[kUQBeginA]);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -276,173 +325,178 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // Global tile sequence t over this CTA's units.  For tile t it issues, in order:
-    // S(t+1) = Q K(t+1)^T (lookahead, also across a unit boundary), then
-    // O += P(t) V(t) once the softmax has written P(t).
+    // Step j of a unit (K/V block kv = it + j): for tile A then tile B (while it has
+    // blocks): O += P(j) V(j), then S = Q K(j+1)^T.  At the unit's last step the
+    // next Q K^T is the next unit's block 0 (same K/V ring, next Q slots), so the
+    // softmax warps start the next unit while this one drains.
     if (lane == 0 && u_begin < u_end) {
-      const uint32_t q_addr = smem_u32(smem + OFF_Q);
-      const uint32_t k_addr = smem_u32(smem + OFF_K);
-      const uint32_t v_addr = smem_u32(smem + OFF_V);
-      const uint32_t o_tmem = tmem_base + TMEM_O;
-      // cursor of the lookahead tile
-      int ui = u_begin, j = 0, na = 0;
-      auto unit_na = [&](int uu) {
-        const int32_t* u = p.units + (int64_t)uu * kUnitInts;
-        return u[kUKbEnd] - u[kUKbBegin];
+      const uint32_t q_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_Q), 16);
+      const uint32_t k_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_K), 16);
+      const uint32_t v_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_V), HALF_BYTES);
+      constexpr uint32_t kTileLo = TILE_BYTES >> 4;  // one tile in descriptor address units
+      int qload = 0;  // Q loads consumed (slot = load % QSLOTS, same order as the Q producer)
+      struct Cur {
+        UnitView v;
+        int load_a, load_b;
       };
-      // Issue S(t) for the tile at cursor (ui, j); returns false on abort.
-      auto issue_s = [&](int t, int uu, int jj, int nn) -> bool {
-        const int lu = uu - u_begin;
-        if (jj == 0) {
-          if (!wait_or_abort(bars.q_full + (lu & 1), (uint32_t)(lu >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 6, abort_flag))
-            return false;
-        }
-        const int s = t % STAGES;
-        if (!wait_or_abort(bars.k_full + s, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 7, abort_flag))
+      auto next_unit = [&](int ui) {
+        Cur c;
+        c.v = unit_view(p.units + (int64_t)ui * kUnitInts);
+        c.load_a = qload++;
+        c.load_b = c.v.n_b > 0 ? qload++ : -1;
+        return c;
+      };
+      auto wait_k = [&](int kv) {
+        return wait_or_abort(bars.k_full + kv % STAGES, (uint32_t)(kv / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 7,
+                             abort_flag);
+      };
+      // S_x = Q(load) K(kv)^T; `first`: the tile's first block (wait for its Q),
+      // `last`: its last block (release the Q slot once the MMA completes).
+      auto qk = [&](int x, int load, int kv, bool first, bool last) {
+        const int slot = load % QSLOTS;
+        if (first && !wait_or_abort(bars.q_full + slot, (uint32_t)(load / QSLOTS) & 1u, VLC_DEV_ERR_TIMEOUT + 6,
+                                    abort_flag))
           return false;
         tc_fence_after();
-        issue_qk(tmem_base + TMEM_S + (t & 1) * 128, q_addr + (lu & 1) * TILE_BYTES, k_addr + s * TILE_BYTES);
-        umma_commit(bars.s_full + (t & 1));
-        umma_commit(bars.k_empty + s);
-        if (jj == nn - 1) umma_commit(bars.q_empty + (lu & 1));
+        issue_qk(tmem_base + TMEM_S + x * 128, q_lo + slot * kTileLo, k_lo + (kv % STAGES) * kTileLo);
+        umma_commit(bars.s_full + x);
+        if (last) umma_commit(bars.q_empty + slot);
         return true;
       };
-      na = unit_na(ui);
-      bool ok = issue_s(0, ui, 0, na);
-      int t = 0;
-      while (ok) {
-        // cursor (ui, j) is tile t; find tile t+1
-        int un = ui, jn = j + 1, nn = na;
-        if (jn == na) {
-          un = ui + 1;
-          jn = 0;
-          nn = un < u_end ? unit_na(un) : 0;
+      Cur cur = next_unit(u_begin);
+      bool ok = wait_k(0) && qk(0, cur.load_a, 0, true, cur.v.n_a == 1) &&
+                (cur.v.n_b == 0 || qk(1, cur.load_b, 0, true, cur.v.n_b == 1));
+      if (ok) umma_commit(bars.k_empty + 0);
+      int pv_a = 0, pv_b = 0;  // P*V issued per tile (p_lo / p_hi phases)
+      int it = 0;              // K/V block index of the current unit's block 0
+      for (int ui = u_begin; ok && ui < u_end; ++ui) {
+        const bool has_next = ui + 1 < u_end;
+        Cur nxt{};
+        if (has_next) nxt = next_unit(ui + 1);
+        for (int j = 0; j < cur.v.n_a; ++j) {
+          const int kv = it + j, s = kv % STAGES;
+          const bool last = j == cur.v.n_a - 1;
+          const bool more = !last || has_next;  // a block kv + 1 follows
+          // tile A
+          if (!wait_or_abort(bars.p_lo + 0, (uint32_t)pv_a & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag) ||
+              !wait_or_abort(bars.v_full + s, (uint32_t)(kv / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv_half(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 0, j > 0);
+          if (!wait_or_abort(bars.p_hi + 0, (uint32_t)pv_a & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv_half(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 1, true);
+          ++pv_a;
+          if (last) umma_commit(bars.o_done + 0);
+          if (more && !wait_k(kv + 1)) {
+            ok = false;
+            break;
+          }
+          if (!last)
+            ok = qk(0, cur.load_a, kv + 1, false, j + 1 == cur.v.n_a - 1);
+          else if (has_next)
+            ok = qk(0, nxt.load_a, kv + 1, true, nxt.v.n_a == 1);
+          if (!ok) break;
+          // tile B
+          if (j < cur.v.n_b) {
+            if (!wait_or_abort(bars.p_lo + 1, (uint32_t)pv_b & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv_half(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 0, j > 0);
+            if (!wait_or_abort(bars.p_hi + 1, (uint32_t)pv_b & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv_half(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 1, true);
+            ++pv_b;
+            if (j == cur.v.n_b - 1)
+              umma_commit(bars.o_done + 1);
+            else
+              ok = qk(1, cur.load_b, kv + 1, false, j + 1 == cur.v.n_b - 1);
+            if (!ok) break;
+          }
+          if (last && has_next && nxt.v.n_b > 0) {
+            ok = qk(1, nxt.load_b, kv + 1, true, nxt.v.n_b == 1);
+            if (!ok) break;
+          }
+          umma_commit(bars.v_empty + s);
+          if (more) umma_commit(bars.k_empty + (kv + 1) % STAGES);
         }
-        if (un < u_end) ok = issue_s(t + 1, un, jn, nn);
-        if (!ok) break;
-        // O += P(t) V(t)
-        const int s = t % STAGES;
-        if (!wait_or_abort(bars.p_full + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag) ||
-            !wait_or_abort(bars.v_full + s, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag))
-          break;
-        tc_fence_after();
-        issue_pv(o_tmem, tmem_base + TMEM_S + (t & 1) * 128, v_addr + s * TILE_BYTES, j > 0);
-        umma_commit(bars.v_empty + s);
-        umma_commit(bars.o_done + (t & 1));
-        ++t;
-        ui = un;
-        j = jn;
-        na = nn;
-        if (ui >= u_end) break;
+        it += cur.v.n_a;
+        cur = nxt;
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax (two column halves)
-    const int h = warp >> 2;            // 0: columns 0-63, 1: columns 64-127
+    // ------------------------------------------------------------ softmax (one warpgroup per tile)
+    const int x = warp >> 2;            // 0: tile A, 1: tile B
     const int row = threadIdx.x & 127;  // == TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t o_addr = tmem_base + lane_off + TMEM_O + h * 64;
-    float* xmax = reinterpret_cast<float*>(smem + OFF_X);   // [parity][half][row]
-    float* xsum = reinterpret_cast<float*>(smem + OFF_L);   // [half][row]
-    int t = 0;  // global tile counter
+    const uint32_t s_addr = tmem_base + lane_off + TMEM_S + x * 128;
+    const uint32_t o_addr = tmem_base + lane_off + TMEM_O + x * 128;
+    int t = 0;      // blocks of this tile processed (s_full / p_lo / p_hi phases)
+    int nunit = 0;  // units of this tile finished (o_done phases)
     for (int ui = u_begin; ui < u_end; ++ui) {
       const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-      const int lu = ui - u_begin;
+      const UnitView uv = unit_view(u);
+      const int n = x == 0 ? uv.n_a : uv.n_b;
+      if (n == 0) continue;
       const int g = u[kUKvHead];
       const int kb0 = u[kUKbBegin];
-      const int n = u[kUKbEnd] - kb0;
       const int kv_len = u[kUKvLen];
-      const int q_begin = u[kUQBeginA], q_count = u[kUQCountA];
-      const int kpos0 = u[kUKpos0A];
-      const int part = u[kUPartA];
+      const int q_begin = u[x == 0 ? kUQBeginA : kUQBeginB];
+      const int q_count = u[x == 0 ? kUQCountA : kUQCountB];
+      const int kpos0 = u[x == 0 ? kUKpos0A : kUKpos0B];
+      const int part = u[x == 0 ? kUPartA : kUPartB];
       const int tok = row / p.group;
       const bool row_valid = row < p.rows && tok < q_count;
       const int qpos = kpos0 + tok;
       float m_use = -INFINITY;
-      float l_part = 0.f;   // this half's share of the row sum
+      float l_row = 0.f;
       bool ok = true;
       for (int j = 0; j < n; ++j, ++t) {
-        const uint32_t s_addr = tmem_base + lane_off + TMEM_S + (t & 1) * 128;
-        if (!wait_or_abort(bars.s_full + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 9, abort_flag)) {
+        if (!wait_or_abort(bars.s_full + x, (uint32_t)t & 1u, VLC_DEV_ERR_TIMEOUT + 9, abort_flag)) {
           ok = false;
           break;
         }
         __syncwarp();
         tc_fence_after();
         const int key0 = (kb0 + j) * BN;
-        uint32_t sr[64];
-        tmem_ld32(s_addr + h * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tmem_ld32(s_addr + h * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        tmem_wait_ld();
-        if (key0 + BN - 1 > kpos0) {  // tile touches the causal diagonal
-          const int lim = qpos - key0 - h * 64;
+        uint32_t sr[128];
 #pragma unroll
-          for (int c = 0; c < 64; ++c)
+        for (int q = 0; q < 4; ++q) tmem_ld32(s_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[q * 32]));
+        tmem_wait_ld();
+        if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal
+          const int lim = qpos - key0;
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
             if (c > lim) sr[c] = __float_as_uint(-INFINITY);
         }
-        float mx0 = __uint_as_float(sr[0]), mx1 = __uint_as_float(sr[1]);
-        float mx2 = __uint_as_float(sr[2]), mx3 = __uint_as_float(sr[3]);
+        float mx[8];
 #pragma unroll
-        for (int c = 4; c < 64; c += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[c]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[c + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[c + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[c + 3]));
-        }
-        // Exchange the half-row maxima (double-buffered by tile parity).  The barrier
-        // also orders this half's S loads before the other half overwrites S with P.
-        float* xm = xmax + (t & 1) * 2 * BM;
-        xm[h * BM + row] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        tc_fence_before();
-        mbar_arrive(bars.xchg + (t & 1));
-        if (!wait_or_abort(bars.xchg + (t & 1), (uint32_t)(t >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 13, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float m_tile = fmaxf(xm[row], xm[BM + row]) * p.scale_log2;
+        for (int k = 0; k < 8; ++k) mx[k] = __uint_as_float(sr[k]);
+#pragma unroll
+        for (int c = 8; c < 128; c += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], __uint_as_float(sr[c + k]), __uint_as_float(sr[c + 8 + k]));
+        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) *
+                             p.scale_log2;
         // Lazy rescaling: only move the reference max when it grows by > 2^8.
         const bool need = m_tile > m_use + 8.0f;
-        if (__any_sync(0xffffffffu, need && j > 0)) {
-          // O must be stable: wait for the previous tile's P*V.
-          if (!wait_or_abort(bars.o_done + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 10,
-                             abort_flag)) {
-            ok = false;
-            break;
-          }
-          __syncwarp();
-          tc_fence_after();
-          const float m_new = need ? m_tile : m_use;
-          const float f = (need && m_use != -INFINITY) ? fast_exp2(m_use - m_new) : 1.0f;
-#pragma unroll 1
-          for (int cb = 0; cb < 2; ++cb) {
-            uint32_t orr[32];
-            tmem_ld32(o_addr + cb * 32, orr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * f);
-            tmem_st32(o_addr + cb * 32, orr);
-          }
-          l_part *= f;
-          m_use = m_new;
-        } else if (need) {
-          m_use = m_tile;  // first tile of the unit
-        }
+        const float m_new = need ? m_tile : m_use;
+        const float f = (need && m_use != -INFINITY) ? fast_exp2(m_use - m_new) : 1.0f;
+        m_use = m_new;
         const float mref = (m_use == -INFINITY) ? 0.f : m_use;
-        // P = exp2(s * scale_log2 - mref) as bf16 pairs; pair c reuses register c.
-        float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), p.scale_log2, -mref));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), p.scale_log2, -mref));
-          l0 += e0;
-          l1 += e1;
-          sr[c] = pack_bf16x2(e0, e1);
-        }
-        l_part += l0 + l1;
-        tmem_st32(s_addr + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        // Keys past the sequence end: zero their V rows so 0 * garbage stays 0.
-        if (h == 0 && key0 + BN > kv_len) {
+        // Keys past the sequence end: zero their V rows so 0 * garbage stays 0.  Tile A
+        // has every block of the unit, and its P*V runs first.
+        if (x == 0 && key0 + BN > kv_len) {
           const int st = t % STAGES;
           if (!wait_or_abort(bars.v_full + st, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) {
             ok = false;
@@ -460,51 +514,123 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           }
           fence_proxy_async_smem();
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bars.p_full + (t & 1));
+        // P = exp2(s * scale_log2 - mref) as bf16 pairs: key pair (2c, 2c+1) goes to S
+        // column c (its register is free: pair c reads registers 2c and 2c+1 >= c).  Each
+        // half of the keys is released to the MMA as soon as it is in TMEM.
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t negm2 = f2_pack(-mref, -mref);
+        uint64_t lsum = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int base = half * 64 + q * 32;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const uint64_t x2 =
+                  f2_fma(f2_pack(__uint_as_float(sr[base + 2 * c]), __uint_as_float(sr[base + 2 * c + 1])), scale2,
+                         negm2);
+              float e0, e1;
+              if ((c & 3) >= 4 - kFmaExpPairsOf4) {
+                exp2_fma2(x2, e0, e1);
+              } else {
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                e0 = fast_exp2(x0);
+                e1 = fast_exp2(x1);
+              }
+              lsum = f2_add(lsum, f2_pack(e0, e1));
+              sr[base + c] = pack_bf16x2(e0, e1);
+            }
+            tmem_st16(s_addr + (base >> 1), *reinterpret_cast<uint32_t(*)[16]>(&sr[base]));
+          }
+          if (half == 0 && __any_sync(0xffffffffu, f != 1.0f)) {
+            // O (stable: P(j-1) V(j-1) completed before S(j)) follows the moved max
+            // before this block's P V starts.
+#pragma unroll 1
+            for (int cb = 0; cb < 8; ++cb) {
+              uint32_t orr[16];
+              tmem_ld16(o_addr + cb * 16, orr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 16; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * f);
+              tmem_st16(o_addr + cb * 16, orr);
+            }
+            l_row *= f;
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(half == 0 ? bars.p_lo + x : bars.p_hi + x);
+        }
+        {
+          float l0, l1;
+          f2_unpack(lsum, l0, l1);
+          l_row += l0 + l1;
+        }
       }
       if (!ok) break;
       // ---------------------------------------------------------- epilogue
-      xsum[h * BM + row] = l_part;
-      mbar_arrive(bars.xsum);
-      if (!wait_or_abort(bars.xsum, (uint32_t)lu & 1u, VLC_DEV_ERR_TIMEOUT + 14, abort_flag)) break;
-      const float l_sum = xsum[row] + xsum[BM + row];
-      if (!wait_or_abort(bars.o_done + ((t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 12,
-                         abort_flag))
-        break;
+      if (!wait_or_abort(bars.o_done + x, (uint32_t)nunit & 1u, VLC_DEV_ERR_TIMEOUT + 12, abort_flag)) break;
+      ++nunit;
       __syncwarp();
       tc_fence_after();
-      const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
+      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
       __nv_bfloat16* dst;
       if (part < 0) {
         const int head = g * p.group + (row - tok * p.group);
-        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * HD + h * 64;
+        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * HD;
       } else {
         // Split partial: O / l as bf16 (the merge re-weights by l and the max).
-        dst = p.part_o + ((int64_t)part * BM + row) * HD + h * 64;
-        if (h == 0) reinterpret_cast<float2*>(p.part_ml)[(int64_t)part * BM + row] = make_float2(m_use, l_sum);
+        dst = p.part_o + ((int64_t)part * BM + row) * HD;
+        reinterpret_cast<float2*>(p.part_ml)[(int64_t)part * BM + row] = make_float2(m_use, l_row);
       }
       const bool store = part < 0 ? row_valid : true;
-#pragma unroll 1
-      for (int cb = 0; cb < 2; ++cb) {
-        uint32_t orr[32];
-        tmem_ld32(o_addr + cb * 32, orr);
-        tmem_wait_ld();
-        if (store) {
+      uint32_t orr[128];
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 0]) * inv, __uint_as_float(orr[c8 * 8 + 1]) * inv);
-            pk.y = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 2]) * inv, __uint_as_float(orr[c8 * 8 + 3]) * inv);
-            pk.z = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 4]) * inv, __uint_as_float(orr[c8 * 8 + 5]) * inv);
-            pk.w = pack_bf16x2(__uint_as_float(orr[c8 * 8 + 6]) * inv, __uint_as_float(orr[c8 * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + cb * 32 + c8 * 8) = pk;
+      for (int q = 0; q < 4; ++q) tmem_ld32(o_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[q * 32]));
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 64; ++c)
+        orr[c] = pack_bf16x2(__uint_as_float(orr[2 * c]) * inv, __uint_as_float(orr[2 * c + 1]) * inv);
+      if (part >= 0 || q_count == p.tokens_per_tile) {
+        // Full tile or split partial: stage 64 columns at a time in shared memory
+        // (128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) and let
+        // one thread write them with a TMA tensor store.
+        uint8_t* stg = smem + OFF_STG + x * STG_TILE;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          if (row == 0) bulk_wait_read_all();  // the previous store has read the buffer
+          named_bar_sync(1 + x, kTileThreads);
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stg + row * 128 + ((c ^ (row & 7)) << 4)) =
+                make_uint4(orr[32 * r + 4 * c], orr[32 * r + 4 * c + 1], orr[32 * r + 4 * c + 2],
+                           orr[32 * r + 4 * c + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(1 + x, kTileThreads);
+          if (row == 0) {
+            if (part < 0)
+              tma_store_3d(&p.tm_o, stg, 64 * r, g * p.group, q_begin);
+            else
+              tma_store_2d(&p.tm_p, stg, 64 * r, part * BM);
+            bulk_commit_group();
           }
+        }
+      } else if (store) {
+        // Last, partial tile of a sequence: the tensor store would write the rows of
+        // the following tokens, so each valid row is written directly.
+        if (p.out_store32) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) st_global_v8(dst + c * 16, *reinterpret_cast<const uint32_t(*)[8]>(&orr[c * 8]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(orr[4 * c], orr[4 * c + 1], orr[4 * c + 2], orr[4 * c + 3]);
         }
       }
       tc_fence_before();
     }
+    if (row == 0) bulk_wait_all();  // this tile's output stores are complete
   }
 
   __syncthreads();
@@ -516,66 +642,89 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 
 // Merge split units.  Part p holds O_p / l_p (bf16), its max m_p and sum l_p:
 //   O = sum_p w_p (O_p / l_p) / sum_p w_p,   w_p = 2^(m_p - M) l_p.
-// One warp per tile row (8 rows per 256-thread block, every row of every merge in
-// flight at once); lane p reads part p's (m, l) so the weights take one round of
-// shuffles, and each lane accumulates 4 of the 128 dims over the parts with
-// independent loads.
-constexpr int kMergeRowsPerBlock = 8;
-
-__global__ void __launch_bounds__(256) prefill_merge_kernel(const int32_t* __restrict__ merges,
-                                                            const __nv_bfloat16* __restrict__ part_o,
-                                                            const float* __restrict__ part_ml,
-                                                            int group, int rows, int blocks_per_merge,
-                                                            __nv_bfloat16* __restrict__ out,
-                                                            int64_t out_token_stride) {
-  const int mi = blockIdx.x / blocks_per_merge;
-  const int row = (blockIdx.x - mi * blocks_per_merge) * kMergeRowsPerBlock + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int32_t* m = merges + (int64_t)mi * kMergeInts;
-  const int q_begin = __ldg(m + kMQBegin), q_count = __ldg(m + kMQCount), g = __ldg(m + kMKvHead);
+// 256-thread blocks listed by the planner as (merge, first row).  A warp is 4
+// groups of 8 lanes; lane c of a group owns dims [16 c, 16 c + 16) (one 32-byte
+// load per part).  With R rows per warp (4, 2 or 1) each row has K = 4 / R groups,
+// group k folding parts k, k + K, ... with a running max (a part's loads do not
+// depend on the running state, so consecutive parts are in flight together); the
+// K states of a row combine through shuffles.
+__global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __restrict__ merges,
+                                                               const int32_t* __restrict__ blocks,
+                                                               const __nv_bfloat16* __restrict__ part_o,
+                                                               const float* __restrict__ part_ml, int group,
+                                                               __nv_bfloat16* __restrict__ out,
+                                                               int64_t out_token_stride) {
+  const int entry = __ldg(blocks + blockIdx.x);
+  const int32_t* m = merges + (int64_t)(entry >> 8) * kMergeInts;
+  const int q_begin = __ldg(m + kMQBegin), g = __ldg(m + kMKvHead);
   const int part0 = __ldg(m + kMPartBegin), nparts = __ldg(m + kMNumParts);
-  if (row >= rows) return;
-  const int tok = row / group;
-  if (tok >= q_count) return;
+  const int R = __ldg(m + kMRowsPerWarp), nrows = __ldg(m + kMRows);
+  const int K = 4 / R;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, c = lane & 7;
+  const int row = (entry & 255) + warp * R + grp / K;
+  const int k0 = grp % K;
+  const bool active = row < nrows;
   const float2* ml = reinterpret_cast<const float2*>(part_ml);
-  // Pass 1: global max over the parts (lanes stride over parts).
-  float M = -INFINITY;
-  for (int i = lane; i < nparts; i += 32) M = fmaxf(M, __ldg(&ml[(int64_t)(part0 + i) * BM + row].x));
+  float acc[16];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float mref = (M == -INFINITY) ? 0.f : M;
-  float L = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int base = 0; base < nparts; base += 32) {
-    float w = 0.f;
-    if (base + lane < nparts) {
-      const float2 v = __ldg(&ml[(int64_t)(part0 + base + lane) * BM + row]);
-      w = (v.x == -INFINITY) ? 0.f : exp2f(v.x - mref) * v.y;  // weight of O_p/l_p is 2^(m_p-M) l_p
-      L += w;
-    }
-    const int n = min(32, nparts - base);
+  for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+  float m_run = -INFINITY, L = 0.f;
+  if (active) {
 #pragma unroll 4
-    for (int i = 0; i < n; ++i) {
-      const float wi = __shfl_sync(0xffffffffu, w, i);
-      if (wi == 0.f) continue;  // empty or fully masked part (its O may be unwritten)
-      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(part_o + ((int64_t)(part0 + base + i) * BM + row) * HD) + lane);
-      const float2 o01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-      const float2 o23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-      acc.x += wi * o01.x;
-      acc.y += wi * o01.y;
-      acc.z += wi * o23.x;
-      acc.w += wi * o23.y;
+    for (int i = k0; i < nparts; i += K) {
+      const int64_t pr = (int64_t)(part0 + i) * BM + row;
+      const float2 v = __ldg(&ml[pr]);
+      const uint4* src = reinterpret_cast<const uint4*>(part_o + pr * HD) + 2 * c;
+      const uint4 r0 = __ldg(src), r1 = __ldg(src + 1);
+      const float m_new = fmaxf(m_run, v.x);
+      const float mr = m_new == -INFINITY ? 0.f : m_new;
+      const float a = fast_exp2(m_run - mr);      // 0 while nothing is accumulated
+      const float w = fast_exp2(v.x - mr) * v.y;  // weight of O_p / l_p (0 for an empty part)
+      m_run = m_new;
+      L = fmaf(L, a, w);
+      const uint32_t wds[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wds[k]));
+        acc[2 * k] = fmaf(w, o.x, acc[2 * k] * a);
+        acc[2 * k + 1] = fmaf(w, o.y, acc[2 * k + 1] * a);
+      }
     }
   }
+  // Combine the K groups of a row (lanes 8 apart): xor 8 when K >= 2, then 16 when K == 4.
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  for (int sh = 8; sh <= 16; sh <<= 1) {
+    if (sh == 8 ? K < 2 : K < 4) break;
+    const float m_oth = __shfl_xor_sync(0xffffffffu, m_run, sh);
+    const float m_all = fmaxf(m_run, m_oth);
+    const float mr = m_all == -INFINITY ? 0.f : m_all;
+    const float a = fast_exp2(m_run - mr);
+    L *= a;
+    L += __shfl_xor_sync(0xffffffffu, L, sh);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      acc[k] *= a;
+      acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], sh);
+    }
+    m_run = m_all;
+  }
+  if (!active || k0 != 0) return;
   const float inv = L > 0.f ? 1.0f / L : 0.f;
+  const int tok = row / group;
   const int head = g * group + (row - tok * group);
-  __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * HD + lane * 4;
-  uint2 pk;
-  pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-  pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2*>(dst) = pk;
+  __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * HD + c * 16;
+  uint4 p0, p1;
+  p0.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  p0.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  p0.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  p0.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+  p1.x = pack_bf16x2(acc[8] * inv, acc[9] * inv);
+  p1.y = pack_bf16x2(acc[10] * inv, acc[11] * inv);
+  p1.z = pack_bf16x2(acc[12] * inv, acc[13] * inv);
+  p1.w = pack_bf16x2(acc[14] * inv, acc[15] * inv);
+  reinterpret_cast<uint4*>(dst)[0] = p0;
+  reinterpret_cast<uint4*>(dst)[1] = p1;
 }
 
 }  // namespace prefill
@@ -635,6 +784,12 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, ks, box, true) != VLC_OK) return VLC_ERR_CUDA;
     if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, vs, box, true) != VLC_OK) return VLC_ERR_CUDA;
   }
+  {
+    const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_heads, (uint64_t)total_q};
+    const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)out_token_stride * 2};
+    const uint32_t box[3] = {64, (uint32_t)group, (uint32_t)T};
+    if (encode_tmap_bf16(&prm.tm_o, out, 3, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+  }
   prm.cta_offsets = plan_dev + plan_host[kPOffCta];
   prm.units = plan_dev + plan_host[kPOffUnits];
   prm.block_tables = block_tables;
@@ -646,9 +801,20 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   prm.num_slots = num_slots;
   prm.out = (__nv_bfloat16*)out;
   prm.out_token_stride = out_token_stride;
+  prm.out_store32 = ((uintptr_t)out % 32 == 0) && (out_token_stride % 16 == 0);
   const int64_t parts = plan_host[kPNumParts];
+  if (ws_need > 0 && (uintptr_t)workspace % 256 != 0) return VLC_ERR_ALIGN;
   prm.part_ml = (float*)workspace;  // [parts][BM][2] fp32 first (8-byte aligned), then bf16 O
   prm.part_o = workspace ? (__nv_bfloat16*)((float*)workspace + parts * BM * 2) : nullptr;
+  if (parts > 0) {
+    const uint64_t dims[2] = {(uint64_t)HD, (uint64_t)parts * BM};
+    const uint64_t strides[1] = {(uint64_t)HD * 2};
+    const uint32_t box[2] = {64, (uint32_t)BM};
+    if (encode_tmap_bf16(&prm.tm_p, prm.part_o, 2, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+  } else {
+    prm.tm_p = prm.tm_o;  // unused
+  }
+  prm.tokens_per_tile = T;
 
   static bool attr_set = false;
   if (!attr_set) {
@@ -661,11 +827,11 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   prefill_attn_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(prm);
   int rc = launch_status();
   if (rc != VLC_OK) return rc;
-  const int nmerge = plan_host[kPNumMerges];
-  if (nmerge > 0) {
-    const int bpm = (rows + kMergeRowsPerBlock - 1) / kMergeRowsPerBlock;
-    prefill_merge_kernel<<<nmerge * bpm, 32 * kMergeRowsPerBlock, 0, st>>>(
-        plan_dev + plan_host[kPOffMerges], prm.part_o, prm.part_ml, group, rows, bpm, prm.out, out_token_stride);
+  const int mblocks = plan_host[kPMergeBlocks];
+  if (mblocks > 0) {
+    prefill_merge_kernel<<<mblocks, 256, 0, st>>>(plan_dev + plan_host[kPOffMerges],
+                                                  plan_dev + plan_host[kPOffMergeBlocks], prm.part_o,
+                                                  prm.part_ml, group, prm.out, out_token_stride);
     rc = launch_status();
   }
   return rc;
