@@ -151,6 +151,25 @@ def test_prefill_nan_in_unwritten_slots(ops):
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
 
 
+def test_prefill_split_tiles_repeat_launches(ops):
+    """Split tiles (partials merged by the merge kernel): repeated launches on the same
+    workspace give identical results (as every layer of a step reuses it)."""
+    H, Hk = 16, 2
+    case = make_warm_case([(20, 4000, 48, 400)], H, Hk, device="cuda", seed=21)
+    plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, Hk, device="cuda", num_sms=16)
+    assert plan.num_merges > 0
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device="cuda")
+    outs = [ops.prefill_attention(case.q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale,
+                                  workspace=ws) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    ref = oatt.prefill_attention(case.q.cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    mx, mean = attn_errors(outs[0], ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
 def test_prefill_cfg2_full_size(ops):
     """BASELINE config 2 (3B, 4K image, 10% recompute): 1,123 query rows x 10,617 keys."""
     H, Hk = 16, 2
