@@ -137,8 +137,10 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// The smem sources of this thread's committed bulk stores have been read.
+// The smem sources of this thread's committed bulk stores have been read (all, or all
+// but the most recent group).
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_allbut1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // This thread's committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 

@@ -462,8 +462,8 @@ extern "C" int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs
     const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_kv_heads, (uint64_t)num_slots};
     const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)num_kv_heads * HD * 2};
     const uint32_t box[3] = {64, 1, (uint32_t)CHUNK};
-    if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
-    if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   prm.q = (const __nv_bfloat16*)q;
   prm.q_seq_stride = q_seq_stride;

@@ -54,8 +54,9 @@ constexpr int TILE_BYTES = 2 * HALF_BYTES;  // 32 KB: full 128 x 128 bf16 tile
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + QSLOTS * TILE_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr int OFF_STG = OFF_V + STAGES * TILE_BYTES;  // epilogue staging: 64 output columns per tile
-constexpr int STG_TILE = HALF_BYTES;                   // 128 rows x 128 B, 128-byte swizzle
+constexpr int OFF_STG = OFF_V + STAGES * TILE_BYTES;  // epilogue staging, per tile two buffers of
+constexpr int STG_BUF = BM * 64;                       // 32 output columns (128 rows x 64 B, 64-byte swizzle)
+constexpr int STG_TILE = 2 * STG_BUF;
 constexpr int OFF_BAR = OFF_STG + 2 * STG_TILE;
 // barriers: q_full[3], q_empty[3], k_full[S], k_empty[S], v_full[S], v_empty[S],
 //           s_full[2], p_lo[2], p_hi[2], o_done[2] (index = tile: 0 A, 1 B).  p_lo: P of
@@ -593,26 +594,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       for (int c = 0; c < 64; ++c)
         orr[c] = pack_bf16x2(__uint_as_float(orr[2 * c]) * inv, __uint_as_float(orr[2 * c + 1]) * inv);
       if (part >= 0 || q_count == p.tokens_per_tile) {
-        // Full tile or split partial: stage 64 columns at a time in shared memory
-        // (128-byte swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) and let
-        // one thread write them with a TMA tensor store.
+        // Full tile or split partial: stage 32 columns at a time in shared memory,
+        // alternating two buffers (64-byte swizzle: 16-byte chunk c of row r at chunk
+        // c ^ ((r / 2) % 4)), and let one thread write each with a TMA tensor store.
         uint8_t* stg = smem + OFF_STG + x * STG_TILE;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          if (row == 0) bulk_wait_read_all();  // the previous store has read the buffer
+        for (int r = 0; r < 4; ++r) {
+          uint8_t* buf = stg + (r & 1) * STG_BUF;
+          if (row == 0) bulk_wait_read_allbut1();  // the store that used this buffer has read it
           named_bar_sync(1 + x, kTileThreads);
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(stg + row * 128 + ((c ^ (row & 7)) << 4)) =
-                make_uint4(orr[32 * r + 4 * c], orr[32 * r + 4 * c + 1], orr[32 * r + 4 * c + 2],
-                           orr[32 * r + 4 * c + 3]);
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4)) =
+                make_uint4(orr[16 * r + 4 * c], orr[16 * r + 4 * c + 1], orr[16 * r + 4 * c + 2],
+                           orr[16 * r + 4 * c + 3]);
           fence_proxy_async_smem();
           named_bar_sync(1 + x, kTileThreads);
           if (row == 0) {
             if (part < 0)
-              tma_store_3d(&p.tm_o, stg, 64 * r, g * p.group, q_begin);
+              tma_store_3d(&p.tm_o, buf, 32 * r, g * p.group, q_begin);
             else
-              tma_store_2d(&p.tm_p, stg, 64 * r, part * BM);
+              tma_store_2d(&p.tm_p, buf, 32 * r, part * BM);
             bulk_commit_group();
           }
         }
@@ -774,21 +776,21 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_heads, (uint64_t)total_q};
     const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)q_token_stride * 2};
     const uint32_t box[3] = {64, (uint32_t)group, (uint32_t)T};
-    if (encode_tmap_bf16(&prm.tm_q, q, 3, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_q, q, 3, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   {
     const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_kv_heads, (uint64_t)num_slots};
     const uint64_t ks[2] = {(uint64_t)HD * 2, (uint64_t)k_row_stride * 2};
     const uint64_t vs[2] = {(uint64_t)HD * 2, (uint64_t)v_row_stride * 2};
     const uint32_t box[3] = {64, 1, (uint32_t)BN};
-    if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, ks, box, true) != VLC_OK) return VLC_ERR_CUDA;
-    if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, vs, box, true) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, ks, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, vs, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   {
     const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_heads, (uint64_t)total_q};
     const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)out_token_stride * 2};
-    const uint32_t box[3] = {64, (uint32_t)group, (uint32_t)T};
-    if (encode_tmap_bf16(&prm.tm_o, out, 3, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+    const uint32_t box[3] = {32, (uint32_t)group, (uint32_t)T};
+    if (encode_tmap_bf16(&prm.tm_o, out, 3, dims, strides, box, 64) != VLC_OK) return VLC_ERR_CUDA;
   }
   prm.cta_offsets = plan_dev + plan_host[kPOffCta];
   prm.units = plan_dev + plan_host[kPOffUnits];
@@ -809,8 +811,8 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   if (parts > 0) {
     const uint64_t dims[2] = {(uint64_t)HD, (uint64_t)parts * BM};
     const uint64_t strides[1] = {(uint64_t)HD * 2};
-    const uint32_t box[2] = {64, (uint32_t)BM};
-    if (encode_tmap_bf16(&prm.tm_p, prm.part_o, 2, dims, strides, box, true) != VLC_OK) return VLC_ERR_CUDA;
+    const uint32_t box[2] = {32, (uint32_t)BM};
+    if (encode_tmap_bf16(&prm.tm_p, prm.part_o, 2, dims, strides, box, 64) != VLC_OK) return VLC_ERR_CUDA;
   } else {
     prm.tm_p = prm.tm_o;  // unused
   }
