@@ -84,6 +84,14 @@ __global__ void __launch_bounds__(256) mrope_shift_kernel(
   const int rows_per_block = blockDim.x / threads_per_row;
   const int r_local = threadIdx.x / threads_per_row;
   const int t = threadIdx.x - r_local * threads_per_row;
+  // The cos/sin table in shared memory: threads of a warp index it by their pair chunk,
+  // which the constant bank would serialise.
+  __shared__ float4 s_cs[2][kMaxHalf / 4];
+  for (int i = threadIdx.x; i < half / 4; i += blockDim.x) {
+    s_cs[0][i] = make_float4(tab.c[4 * i], tab.c[4 * i + 1], tab.c[4 * i + 2], tab.c[4 * i + 3]);
+    s_cs[1][i] = make_float4(tab.s[4 * i], tab.s[4 * i + 1], tab.s[4 * i + 2], tab.s[4 * i + 3]);
+  }
+  __syncthreads();
   if (r_local >= rows_per_block) return;
   const int row = blockIdx.x * rows_per_block + r_local;
   if (row >= num_rows) return;
@@ -107,10 +115,15 @@ __global__ void __launch_bounds__(256) mrope_shift_kernel(
   float x1[8], x2[8], y1[8], y2[8];
   unpack8(u1, x1);
   unpack8(u2, x2);
+  float csv[8], snv[8];
+  *reinterpret_cast<float4*>(&csv[0]) = s_cs[0][2 * c];
+  *reinterpret_cast<float4*>(&csv[4]) = s_cs[0][2 * c + 1];
+  *reinterpret_cast<float4*>(&snv[0]) = s_cs[1][2 * c];
+  *reinterpret_cast<float4*>(&snv[4]) = s_cs[1][2 * c + 1];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float cs = tab.c[c * 8 + i];
-    const float sn = tab.s[c * 8 + i];
+    const float cs = csv[i];
+    const float sn = snv[i];
     const float t1 = __fmul_rn(x2[i], sn);
     const float t2 = __fmul_rn(x1[i], sn);
     y1[i] = __fmaf_rn(x1[i], cs, -t1);
