@@ -314,6 +314,53 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
     return ms, h2d_bytes, d2h_bytes
 
 
+# ---------------------------------------------------------------------------- metadata
+def metadata_bench(device, reps: int = 20):
+    """Warm-prefill metadata for a BASELINE config 3 batch (64 warm requests sharing a
+    1920x1080 image, prefix U[0,512], suffix U[16,128], ratio 0.05, plus the image-reuse
+    slots): the vectorised host builder vs the device builder (descriptor upload + one
+    kernel), wall time per batch, median of ``reps``."""
+    from vlcache_b200.engine import kv_cache as kvc
+    rng = np.random.default_rng(3)
+    n_img = 39 * 69
+    R3 = kvc.recompute_count(0.05, n_img)
+    reqs, reuse, page = [], [], 0
+    for i in range(64):
+        pre, suf = int(rng.integers(0, 513)), int(rng.integers(16, 129))
+        n = pre + n_img + suf
+        nb = (n + BLOCK - 1) // BLOCK
+        reqs.append(kvc.WarmRequest(n, list(range(page, page + nb)), pre, pre + n_img, R3, True))
+        page += nb
+        reuse.append(kvc.ImageReuse(i, 5, list(range(100000, 100000 + 12))))
+    builder = kvc.WarmPrefillBuilder(H, HK)
+
+    def host():
+        b = builder.build(reqs)
+        for it in reuse:
+            r = reqs[it.request]
+            kvc.image_reuse_slots(r.img_start, r.img_end, r.num_recompute, r.block_table, it.old_img_start,
+                                  it.old_block_table)
+        return b
+
+    def dev():
+        builder.build_device(reqs, reuse, device=device, install=False)
+        torch.cuda.synchronize()
+
+    out = {}
+    for name, fn in (("host_us", host), ("device_us", dev)):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append((time.perf_counter() - t0) * 1e6)
+        out[name] = statistics.median(ts)
+    q_rows = int(builder.build(reqs).cu_seqlens_q[-1])
+    return {"workload": f"cfg3: 64 warm requests, {q_rows} query rows, "
+                        f"{64 * (n_img - R3)} reused image rows", **out}
+
+
 # ---------------------------------------------------------------------------- decode
 def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_graph=True):
     from vlcache_b200 import ops
@@ -511,6 +558,7 @@ def main():
     del step_graph, attn_graph, wl
     torch.cuda.empty_cache()
     dec_us, dec_gbs, dec_bytes = decode_bench(device, args.steps, warmup, dist_on)
+    meta = metadata_bench(device) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -542,6 +590,7 @@ def main():
                        "us_per_layer": dec_us, "hbm_gbs": dec_gbs, "frac": dec_gbs / hbm_peak,
                        "bytes_per_layer": dec_bytes, "peak_gbs": hbm_peak},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "metadata": meta,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
             "device_error": err,

@@ -179,6 +179,30 @@ int vlc_decode_attn_noalloc(const void* q, int64_t q_seq_stride, int num_seqs, i
 /* Size in bytes of the built-in scratch array used by vlc_decode_attn_noalloc. */
 int64_t vlc_decode_noalloc_scratch_bytes(void);
 
+/* --------------------------------------------------------------------------
+ * Warm-prefill metadata on the device.  Replaces the O(tokens) host loops of
+ * nanovllm/engine/model_runner.py:160-168 (_compute_slots), :182-192 (padded block
+ * tables), :232-276 (warm branch of prepare_prefill: positions, slot_mapping) and
+ * nanovllm/engine/llm_engine.py:75-89 (_do_image_kv_copy: old/new slots of the
+ * reused image rows).  The host lists O(requests) descriptors (device int32):
+ *   vseq_desc[num_vseqs][7]  = {q_begin, q_len, first position, block-table offset
+ *                               into block_tables_flat, block-table length, first
+ *                               slot_mapping row (-1: none), output block-table row
+ *                               (-1: none)}; a warm request is two virtual sequences,
+ *                               [0, img_start + R) and [img_end, seqlen);
+ *   reuse_desc[num_reuse][8] = {output offset, rows, first new position, new table
+ *                               offset, new table length, first old position, old
+ *                               table offset, old table length}.
+ * Outputs (device; positions / slot_mapping / block_tables may be NULL):
+ *   positions[q] (int64), slot_mapping[q] (int32), block_tables[num_vseqs][width]
+ *   (int32, -1 padded), src_slots / dst_slots[rows] (int32).
+ * slot(p) = table[p / block_size] * block_size + p % block_size; a page index past
+ * the table's length writes -1 and records VLC_DEV_ERR_BLOCK_RANGE.  One launch. */
+int vlc_warm_metadata(const int32_t* vseq_desc, int num_vseqs, const int32_t* reuse_desc, int num_reuse,
+                      const int32_t* block_tables_flat, int block_size, int64_t* positions,
+                      int32_t* slot_mapping, int32_t* block_tables, int block_table_width,
+                      int32_t* src_slots, int32_t* dst_slots, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

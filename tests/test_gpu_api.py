@@ -201,3 +201,86 @@ def test_prefill_cfg4_ratio_002_7b(api):
                                  case.cu_q, case.cu_k, case.scale)
     mx, mean = attn_errors(out, ref)
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
+# ------------------------------------------------------------------ device metadata builder
+def _golden_reqs(name):
+    from pathlib import Path
+    from vlcache_b200.engine import kv_cache as kvc
+    g = dict(np.load(Path(__file__).resolve().parent / "golden" / f"metadata_{name}.npz"))
+    reqs = []
+    for i, (n, s, e, R, partial) in enumerate(g["requests"]):
+        bt = [int(x) for x in g["request_block_tables"][i] if x >= 0]
+        reqs.append(kvc.WarmRequest(int(n), bt, int(s) if s >= 0 else None, int(e) if e >= 0 else None, int(R),
+                                    bool(partial)))
+    reuse = [kvc.ImageReuse(i, int(g["cold_img_start"]), [int(x) for x in g["cold_block_table"]])
+             for i, r in enumerate(reqs) if r.partial]
+    return g, reqs, reuse
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "mixed"])
+def test_device_metadata_matches_reference_fixtures(api, name):
+    """The device builder reproduces, bit for bit, the metadata the reference's own
+    prepare_prefill / _do_image_kv_copy produced for these batches (golden fixtures)."""
+    ops, kvc, Attention, ctx = api
+    g, reqs, reuse = _golden_reqs(name)
+    b = kvc.WarmPrefillBuilder(16, 2).build_device(reqs, reuse, device="cuda", install=False)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    t = b.device_tensors
+    assert np.array_equal(b.cu_seqlens_q, g["cu_seqlens_q"]) and np.array_equal(b.cu_seqlens_k, g["cu_seqlens_k"])
+    assert np.array_equal(t["positions"].cpu().numpy(), g["positions"])
+    assert np.array_equal(t["slot_mapping"].cpu().numpy(), g["slot_mapping"])
+    assert np.array_equal(t["block_tables"].cpu().numpy(), g["block_tables"])
+    assert list(b.logit_indices) == list(g["logit_indices"])
+    assert np.array_equal(t["reuse_src"].cpu().numpy(), g["old_slots"])
+    assert np.array_equal(t["reuse_dst"].cpu().numpy(), g["new_slots"])
+
+
+def test_device_metadata_matches_host_builder_cfg3_batch(api):
+    """64 warm requests of BASELINE config 3 shape (plus two cold ones): device and host
+    builders agree on every array, and the reuse slots equal image_reuse_slots."""
+    ops, kvc, Attention, ctx = api
+    rng = np.random.default_rng(31)
+    n_img, R = 39 * 69, kvc.recompute_count(0.05, 39 * 69)
+    reqs, reuse, next_page = [], [], 0
+    for i in range(66):
+        pre, suf = int(rng.integers(0, 513)), int(rng.integers(16, 129))
+        n = pre + n_img + suf if i < 64 else int(rng.integers(1, 3000))
+        nb = (n + 255) // 256
+        bt = list(range(next_page, next_page + nb))
+        next_page += nb
+        if i < 64:
+            reqs.append(kvc.WarmRequest(n, bt, pre, pre + n_img, R, True))
+            reuse.append(kvc.ImageReuse(i, 7, list(range(900000, 900000 + 12))))
+        else:
+            reqs.append(kvc.WarmRequest(n, bt))
+    builder = kvc.WarmPrefillBuilder(16, 2)
+    host = builder.build(reqs)
+    dev = builder.build_device(reqs, reuse, device="cuda", install=False)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    t = dev.device_tensors
+    assert np.array_equal(t["positions"].cpu().numpy(), host.positions)
+    assert np.array_equal(t["slot_mapping"].cpu().numpy(), host.slot_mapping)
+    assert np.array_equal(t["block_tables"].cpu().numpy(), host.block_tables)
+    assert np.array_equal(dev.cu_seqlens_q, host.cu_seqlens_q) and np.array_equal(dev.cu_seqlens_k, host.cu_seqlens_k)
+    src = np.concatenate([kvc.image_reuse_slots(reqs[i].img_start, reqs[i].img_end, R, reqs[i].block_table, 7,
+                                                list(range(900000, 900012)))[0] for i in range(64)])
+    dst = np.concatenate([kvc.image_reuse_slots(reqs[i].img_start, reqs[i].img_end, R, reqs[i].block_table, 7,
+                                                list(range(900000, 900012)))[1] for i in range(64)])
+    assert np.array_equal(t["reuse_src"].cpu().numpy(), src)
+    assert np.array_equal(t["reuse_dst"].cpu().numpy(), dst)
+
+
+def test_device_metadata_flags_short_block_table(api):
+    """A block table too short for a request's positions: device error 102, slot -1."""
+    ops, kvc, Attention, ctx = api
+    ops.device_error(reset=True)
+    reqs = [kvc.WarmRequest(700, [3, 5])]          # 700 tokens need 3 pages of 256
+    b = kvc.WarmPrefillBuilder(16, 2).build_device(reqs, device="cuda", install=False)
+    torch.cuda.synchronize()
+    assert ops.device_error(reset=True) == 102
+    s = b.device_tensors["slot_mapping"].cpu().numpy()
+    assert np.array_equal(s[:512], np.concatenate([np.arange(768, 1024), np.arange(1280, 1536)]))
+    assert np.all(s[512:] == -1)

@@ -38,6 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_decode_attn_noalloc": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_int, c_int, c_vp, c_int,
                                         c_int, c_vp, c_int, c_float, c_vp, c_i64, c_vp]),
     "vlc_decode_noalloc_scratch_bytes": (c_i64, []),
+    "vlc_warm_metadata": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp,
+                                  c_vp]),
 }
 
 

@@ -88,13 +88,22 @@ class WarmRequest:
 
 
 @dataclass
+class ImageReuse:
+    """A warm request's reused image rows: where the image sat in the request that cached
+    it (the encoder-cache entry's ``img_start`` and block table)."""
+    request: int
+    old_img_start: int
+    old_block_table: list[int]
+
+
+@dataclass
 class PrefillBatch:
-    positions: np.ndarray
+    positions: np.ndarray | None
     cu_seqlens_q: np.ndarray
     cu_seqlens_k: np.ndarray
     max_seqlen_q: int
     max_seqlen_k: int
-    slot_mapping: np.ndarray
+    slot_mapping: np.ndarray | None
     block_tables: np.ndarray | None
     logit_indices: list[int] | None
     plan: ops.PrefillPlan | None = None
@@ -160,6 +169,92 @@ class WarmPrefillBuilder:
             cu_seqlens_q=cq_a, cu_seqlens_k=ck_a, max_seqlen_q=max_q, max_seqlen_k=max_k,
             slot_mapping=np.concatenate(slots).astype(np.int32) if slots else np.zeros(0, np.int32),
             block_tables=block_tables, logit_indices=logit_indices if any_partial else None)
+
+    def build_device(self, reqs: list[WarmRequest], reuse: list[ImageReuse] = (), device="cuda",
+                     install: bool = True) -> PrefillBatch:
+        """``build`` on the device: the same arrays, bit for bit, from O(requests) host work.
+
+        The host lists one descriptor per virtual sequence (two per warm request) and per
+        reused image, uploads them with the block tables in one pinned copy, and one
+        kernel (vlc_warm_metadata) writes positions, slot_mapping, the padded block tables
+        and the image-reuse source/destination slots.  With ``install`` the attention is
+        planned and the context set, as ``upload`` does.  The device tensors are in
+        ``device_tensors`` (``reuse_src`` / ``reuse_dst`` for the image move)."""
+        vdesc, cq, ck, tables = [], [0], [0], []
+        offsets, lengths = [], []
+        q = slot = row = 0
+        max_q = max_k = width = 0
+        vidx = 0
+        logit_indices: list[int] = []
+        any_partial = False
+        for r in reqs:
+            offsets.append(sum(lengths))
+            lengths.append(len(r.block_table))
+            tables.append(np.asarray(r.block_table, dtype=np.int32))
+        for i, r in enumerate(reqs):
+            n, L, off = r.seqlen, lengths[i], offsets[i]
+            has = L > 0
+            if r.partial:
+                any_partial = True
+                a = r.img_start + r.num_recompute
+                parts = [(a, 0), (n - r.img_end, r.img_end)]
+                cq += [cq[-1] + a, cq[-1] + a + (n - r.img_end)]
+                ck += [ck[-1] + a, ck[-1] + a + n]
+                max_q = max(max_q, a, n - r.img_end)
+                max_k = max(max_k, a, n)
+                logit_indices.append(vidx + 1)
+                vidx += 2
+            else:
+                parts = [(n, 0)]
+                cq.append(cq[-1] + n)
+                ck.append(ck[-1] + n)
+                max_q, max_k = max(max_q, n), max(max_k, n)
+                logit_indices.append(vidx)
+                vidx += 1
+            for qlen, pos0 in parts:
+                vdesc.append([q, qlen, pos0, off, L, slot if has else -1, row if has else -1])
+                q += qlen
+                if has:
+                    slot += qlen
+                    row += 1
+                    width = max(width, L)
+        rdesc, out = [], 0
+        for it in reuse:
+            r = reqs[it.request]
+            count = r.img_end - r.img_start - r.num_recompute
+            old_off = sum(lengths) + sum(len(t) for t in tables[len(reqs):])
+            tables.append(np.asarray(it.old_block_table, dtype=np.int32))
+            rdesc.append([out, count, r.img_start + r.num_recompute, offsets[it.request], lengths[it.request],
+                          it.old_img_start + r.num_recompute, old_off, len(it.old_block_table)])
+            out += count
+        nv, nr = len(vdesc), len(rdesc)
+        flat_tables = np.concatenate(tables) if tables else np.zeros(0, np.int32)
+        desc = np.concatenate([np.asarray(vdesc, np.int32).reshape(-1), np.asarray(rdesc, np.int32).reshape(-1),
+                               flat_tables, np.zeros(1, np.int32)])
+        desc_dev = torch.from_numpy(desc).pin_memory().to(device, non_blocking=True)
+        rows = row if any_partial else 0
+        positions, slots, bt, src, dst = ops.warm_metadata(
+            desc_dev, nv, nv * ops.VSEQ_INTS, nr, nv * ops.VSEQ_INTS + nr * ops.REUSE_INTS, self.block_size, q,
+            slot, rows, width if rows else 0, out)
+        cq_a = np.asarray(cq, dtype=np.int32)
+        ck_a = np.asarray(ck, dtype=np.int32)
+        batch = PrefillBatch(positions=None, cu_seqlens_q=cq_a, cu_seqlens_k=ck_a, max_seqlen_q=max_q,
+                             max_seqlen_k=max_k, slot_mapping=None, block_tables=None,
+                             logit_indices=logit_indices if any_partial else None)
+        batch.device_tensors = {
+            "positions": positions, "slot_mapping": slots, "block_tables": bt, "reuse_src": src, "reuse_dst": dst,
+            "cu_seqlens_q": torch.from_numpy(cq_a).pin_memory().to(device, non_blocking=True),
+            "cu_seqlens_k": torch.from_numpy(ck_a).pin_memory().to(device, non_blocking=True),
+            "descriptors": desc_dev,
+        }
+        if install:
+            t = batch.device_tensors
+            batch.plan = ops.build_prefill_plan(cq_a, ck_a, self.num_heads, self.num_kv_heads, self.head_dim,
+                                                device=device)
+            set_context(True, t["cu_seqlens_q"], t["cu_seqlens_k"], max_q, max_k, t["slot_mapping"], None,
+                        t["block_tables"], prefill_plan=batch.plan, cu_seqlens_q_host=cq_a,
+                        cu_seqlens_k_host=ck_a)
+        return batch
 
     def upload(self, batch: PrefillBatch, device="cuda") -> PrefillBatch:
         """Copy the metadata to the device (pinned, non-blocking), plan the attention

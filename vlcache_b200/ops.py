@@ -232,3 +232,32 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
                                _ptr(workspace), ws_bytes, _stream())
     check("vlc_decode_attn", st)
     return out
+
+
+# --------------------------------------------------------------------------- metadata
+VSEQ_INTS, REUSE_INTS = 7, 8
+
+
+def warm_metadata(desc: torch.Tensor, num_vseqs: int, reuse_offset: int, num_reuse: int, table_offset: int,
+                  block_size: int, total_q: int, total_slots: int, table_rows: int, table_width: int,
+                  total_reuse: int):
+    """Device warm-prefill metadata from one int32 descriptor buffer ``desc`` =
+    [virtual-sequence descriptors][reuse descriptors at reuse_offset][flat block tables at
+    table_offset] (layout in include/vlcache_b200.h, vlc_warm_metadata).  Returns
+    (positions int64, slot_mapping int32, block_tables int32 or None, src_slots, dst_slots)."""
+    _require_cuda(desc)
+    assert desc.dtype == torch.int32 and desc.is_contiguous()
+    dev = desc.device
+    positions = torch.empty(total_q, dtype=torch.int64, device=dev)
+    slots = torch.empty(total_slots, dtype=torch.int32, device=dev)
+    tables = torch.empty(table_rows, table_width, dtype=torch.int32, device=dev) if table_rows > 0 else None
+    src = torch.empty(total_reuse, dtype=torch.int32, device=dev)
+    dst = torch.empty(total_reuse, dtype=torch.int32, device=dev)
+    base = desc.data_ptr()
+    st = lib().vlc_warm_metadata(ctypes.c_void_p(base), num_vseqs, ctypes.c_void_p(base + 4 * reuse_offset),
+                                 num_reuse, ctypes.c_void_p(base + 4 * table_offset), block_size,
+                                 _ptr(positions), _ptr(slots) if total_slots > 0 else ctypes.c_void_p(0),
+                                 _ptr(tables), table_width if tables is not None else 0, _ptr(src), _ptr(dst),
+                                 _stream())
+    check("vlc_warm_metadata", st)
+    return positions, slots, tables, src, dst
