@@ -452,6 +452,25 @@ def run_only(args, device):
     if args.only == "decode":
         us, gbs, nbytes = decode_bench(device, args.steps, max(3, args.warmup), False, distinct=1, use_graph=False)
         res.update(us_per_layer=us, hbm_gbs=gbs, bytes_per_layer=nbytes)
+    elif args.only == "prefill_7b_full":
+        # BASELINE config 4 at ratio 1.0 (7B heads, every one of the 10,617 rows recomputed):
+        # the steady state of the attention pipeline, one layer per launch.
+        from vlcache_b200 import ops
+        n, h7, hk7 = SEQLEN, 28, 4
+        g = torch.Generator(device=device).manual_seed(42)
+        q = torch.randn(n, h7, D, generator=g, device=device).to(torch.bfloat16)
+        kc = torch.randn((n + BLOCK - 1) // BLOCK + 1, BLOCK, hk7, D, generator=g, device=device).to(torch.bfloat16)
+        vc = torch.randn_like(kc)
+        bt = torch.arange(kc.shape[0] - 1, dtype=torch.int32, device=device).view(1, -1)
+        plan = ops.build_prefill_plan([0, n], [0, n], h7, hk7, device=device)
+        out = torch.empty_like(q)
+        scale = 1.0 / math.sqrt(D)
+
+        def fn():
+            ops.prefill_attention(q, kc, vc, bt, plan, scale, out)
+        ms = timed(fn, args.steps, max(3, args.warmup), False)
+        flop = 4 * D * h7 * causal_pairs([0, n], [0, n])
+        res.update(us_per_launch=ms * 1e3, tflops=flop / (ms * 1e-3) / 1e12)
     else:
         wl = WarmPrefillWorkload(device)
         if args.only == "prefill":
@@ -513,7 +532,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "decode", "shift", "scatter"],
+    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -209,3 +209,33 @@ def test_decode_matches_oracle(ops, model, lens):
     assert torch.isfinite(out).all()
     mx, mean = attn_errors(out, ref)
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
+def test_prefill_graph_capture_replay(ops):
+    """The prefill launch (attention + split merge) is capture-safe: a captured CUDA graph
+    replays to the eager result, also after the inputs change in place (as the bench's
+    per-step graph and nano-vllm's graphs use it)."""
+    H, Hk = 16, 2
+    case = make_warm_case([(20, 3000, 48, 300)], H, Hk, device="cuda", seed=23)
+    plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, Hk, device="cuda", num_sms=32)
+    assert plan.num_merges > 0
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(case.q)
+    ops.prefill_attention(case.q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale, out, ws)
+    torch.cuda.synchronize()
+    eager = out.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.prefill_attention(case.q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale, out, ws)
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    case.q.mul_(0.5)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    ref = oatt.prefill_attention(case.q.cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    mx, mean = attn_errors(out, ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
