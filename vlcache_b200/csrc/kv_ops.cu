@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) store_kvcache_kernel(
     int64_t value_stride16, uint4* __restrict__ k_cache, uint4* __restrict__ v_cache,
     const int32_t* __restrict__ slot_mapping, int num_tokens, int chunks_per_row,
     int64_t num_slots) {
+  pdl_launch_dependents();  // the attention that follows may start its prologue
   const int token = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (token >= num_tokens) return;
   const int lane = threadIdx.x & 31;
@@ -73,6 +74,8 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
+constexpr int kShiftRowsPerThread = 2;
+
 __global__ void __launch_bounds__(256) mrope_shift_kernel(
     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
     int64_t layer_stride, int64_t num_slots, int num_kv_heads, int head_dim,
@@ -93,51 +96,62 @@ __global__ void __launch_bounds__(256) mrope_shift_kernel(
   }
   __syncthreads();
   if (r_local >= rows_per_block) return;
-  const int row = blockIdx.x * rows_per_block + r_local;
-  if (row >= num_rows) return;
   const int layer = blockIdx.y;
-
-  const int src = __ldg(src_slots + row);
-  const int dst = dst_slots ? __ldg(dst_slots + row) : src;
-  if (src < 0 || dst < 0 || (int64_t)src >= num_slots || (int64_t)dst >= num_slots) {
-    if (t == 0 && layer == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
-    return;
-  }
   const int head = t / chunks_per_head;
   const int c = t - head * chunks_per_head;
   const int64_t row_elems = (int64_t)num_kv_heads * head_dim;
-  const int64_t lbase = (int64_t)layer * layer_stride;
-  const int64_t so = lbase + (int64_t)src * row_elems + (int64_t)head * head_dim + c * 8;
-  const int64_t dof = lbase + (int64_t)dst * row_elems + (int64_t)head * head_dim + c * 8;
-
-  const uint4 u1 = *reinterpret_cast<const uint4*>(k_cache + so);
-  const uint4 u2 = *reinterpret_cast<const uint4*>(k_cache + so + half);
-  float x1[8], x2[8], y1[8], y2[8];
-  unpack8(u1, x1);
-  unpack8(u2, x2);
+  const int64_t lbase = (int64_t)layer * layer_stride + (int64_t)head * head_dim + c * 8;
+  const bool move_v = v_cache != nullptr && dst_slots != nullptr;
+  // kShiftRowsPerThread rows per thread, every K and V load issued before any math.
+  int64_t so[kShiftRowsPerThread], dof[kShiftRowsPerThread];
+  bool live[kShiftRowsPerThread];
+  uint4 u1[kShiftRowsPerThread], u2[kShiftRowsPerThread], w1[kShiftRowsPerThread], w2[kShiftRowsPerThread];
+#pragma unroll
+  for (int k = 0; k < kShiftRowsPerThread; ++k) {
+    const int row = (blockIdx.x * kShiftRowsPerThread + k) * rows_per_block + r_local;
+    live[k] = row < num_rows;
+    if (!live[k]) continue;
+    const int src = __ldg(src_slots + row);
+    const int dst = dst_slots ? __ldg(dst_slots + row) : src;
+    if (src < 0 || dst < 0 || (int64_t)src >= num_slots || (int64_t)dst >= num_slots) {
+      if (t == 0 && layer == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
+      live[k] = false;
+      continue;
+    }
+    so[k] = lbase + (int64_t)src * row_elems;
+    dof[k] = lbase + (int64_t)dst * row_elems;
+    u1[k] = *reinterpret_cast<const uint4*>(k_cache + so[k]);
+    u2[k] = *reinterpret_cast<const uint4*>(k_cache + so[k] + half);
+    if (move_v) {
+      // the same thread moves the two matching 16-byte chunks of the V row
+      w1[k] = *reinterpret_cast<const uint4*>(v_cache + so[k]);
+      w2[k] = *reinterpret_cast<const uint4*>(v_cache + so[k] + half);
+    }
+  }
   float csv[8], snv[8];
   *reinterpret_cast<float4*>(&csv[0]) = s_cs[0][2 * c];
   *reinterpret_cast<float4*>(&csv[4]) = s_cs[0][2 * c + 1];
   *reinterpret_cast<float4*>(&snv[0]) = s_cs[1][2 * c];
   *reinterpret_cast<float4*>(&snv[4]) = s_cs[1][2 * c + 1];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float cs = csv[i];
-    const float sn = snv[i];
-    const float t1 = __fmul_rn(x2[i], sn);
-    const float t2 = __fmul_rn(x1[i], sn);
-    y1[i] = __fmaf_rn(x1[i], cs, -t1);
-    y2[i] = __fmaf_rn(x2[i], cs, t2);
-  }
-  *reinterpret_cast<uint4*>(k_cache + dof) = pack8(y1);
-  *reinterpret_cast<uint4*>(k_cache + dof + half) = pack8(y2);
-
-  if (v_cache != nullptr && dst_slots != nullptr) {
-    // Same thread copies the two matching 16-byte chunks of the V row.
-    const uint4 w1 = *reinterpret_cast<const uint4*>(v_cache + so);
-    const uint4 w2 = *reinterpret_cast<const uint4*>(v_cache + so + half);
-    *reinterpret_cast<uint4*>(v_cache + dof) = w1;
-    *reinterpret_cast<uint4*>(v_cache + dof + half) = w2;
+  for (int k = 0; k < kShiftRowsPerThread; ++k) {
+    if (!live[k]) continue;
+    float x1[8], x2[8], y1[8], y2[8];
+    unpack8(u1[k], x1);
+    unpack8(u2[k], x2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float t1 = __fmul_rn(x2[i], snv[i]);
+      const float t2 = __fmul_rn(x1[i], snv[i]);
+      y1[i] = __fmaf_rn(x1[i], csv[i], -t1);
+      y2[i] = __fmaf_rn(x2[i], csv[i], t2);
+    }
+    *reinterpret_cast<uint4*>(k_cache + dof[k]) = pack8(y1);
+    *reinterpret_cast<uint4*>(k_cache + dof[k] + half) = pack8(y2);
+    if (move_v) {
+      *reinterpret_cast<uint4*>(v_cache + dof[k]) = w1[k];
+      *reinterpret_cast<uint4*>(v_cache + dof[k] + half) = w2[k];
+    }
   }
 }
 
@@ -198,7 +212,8 @@ extern "C" int vlc_mrope_shift(void* k_cache, void* v_cache, int64_t layer_strid
     tab.s[j] = (float)sin(a);
   }
   const int rows_per_block = 256 / threads_per_row;
-  dim3 grid((num_rows + rows_per_block - 1) / rows_per_block, num_layers);
+  const int rows_per_grid_x = rows_per_block * kShiftRowsPerThread;
+  dim3 grid((num_rows + rows_per_grid_x - 1) / rows_per_grid_x, num_layers);
   mrope_shift_kernel<<<grid, rows_per_block * threads_per_row, 0, (cudaStream_t)stream>>>(
       (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, layer_stride, num_slots, num_kv_heads,
       head_dim, src_slots, dst_slots, num_rows, tab);

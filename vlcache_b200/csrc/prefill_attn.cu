@@ -239,6 +239,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
     }
     fence_mbar_init();
   }
+  if (threadIdx.x == 0) pdl_launch_dependents();  // the merge may be scheduled as SMs free up
   if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
@@ -269,6 +270,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   if (warp == 10) {
     // ------------------------------------------------------------ Q producer
     if (lane == 0) {
+      pdl_wait();  // Q may be written by the preceding kernel
       int load = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         const int32_t* u = p.units + (int64_t)ui * kUnitInts;
@@ -294,6 +296,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   } else if (warp == 8) {
     // ------------------------------------------------------------ K/V producer
     if (lane == 0) {
+      pdl_wait();  // K/V rows are written by the preceding store_kvcache
       int it = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         const int32_t* u = p.units + (int64_t)ui * kUnitInts;
@@ -658,6 +661,7 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
                                                                int64_t out_token_stride) {
   const int entry = __ldg(blocks + blockIdx.x);
   const int32_t* m = merges + (int64_t)(entry >> 8) * kMergeInts;
+  pdl_wait();  // the partials are written by the attention kernel launched just before
   const int q_begin = __ldg(m + kMQBegin), g = __ldg(m + kMKvHead);
   const int part0 = __ldg(m + kMPartBegin), nparts = __ldg(m + kMNumParts);
   const int R = __ldg(m + kMRowsPerWarp), nrows = __ldg(m + kMRows);
@@ -826,15 +830,39 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     attr_set = true;
   }
   cudaStream_t st = (cudaStream_t)stream;
-  prefill_attn_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(prm);
-  int rc = launch_status();
-  if (rc != VLC_OK) return rc;
+  // Both kernels are launched as programmatic dependents of their predecessor in the
+  // stream (the attention: of the KV scatter; the merge: of the attention).  They wait
+  // (griddepcontrol.wait) before reading the predecessor's outputs, so the launch and
+  // prologue overlap its tail.
+  cudaLaunchAttribute pdl;
+  pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = &pdl;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel, prm) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return VLC_ERR_CUDA;
+  }
+  int rc = VLC_OK;
   const int mblocks = plan_host[kPMergeBlocks];
   if (mblocks > 0) {
-    prefill_merge_kernel<<<mblocks, 256, 0, st>>>(plan_dev + plan_host[kPOffMerges],
-                                                  plan_dev + plan_host[kPOffMergeBlocks], prm.part_o,
-                                                  prm.part_ml, group, prm.out, out_token_stride);
-    rc = launch_status();
+    cudaLaunchConfig_t mcfg = {};
+    mcfg.gridDim = dim3(mblocks);
+    mcfg.blockDim = dim3(256);
+    mcfg.stream = st;
+    mcfg.attrs = &pdl;
+    mcfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&mcfg, prefill_merge_kernel, (const int32_t*)(plan_dev + plan_host[kPOffMerges]),
+                           (const int32_t*)(plan_dev + plan_host[kPOffMergeBlocks]), (const __nv_bfloat16*)prm.part_o,
+                           (const float*)prm.part_ml, group, prm.out, out_token_stride) != cudaSuccess) {
+      (void)cudaGetLastError();
+      rc = VLC_ERR_CUDA;
+    }
   }
   return rc;
 }
