@@ -128,6 +128,10 @@ int64_t vlc_prefill_workspace_size(const int32_t* plan_host);
  * plan_host is the same plan on the host (only its header is read).
  * out: [total_q, num_heads, head_dim] bf16 with token stride out_token_stride.
  * head_dim must be 128.
+ * Launch order: the attention is a programmatic dependent launch of the kernel
+ * enqueued just before it on `stream` (its setup overlaps that kernel's tail).
+ * That kernel may write q, k and v; plan_dev and block_tables must have been
+ * written by a copy or by an earlier kernel.
  * ------------------------------------------------------------------------ */
 int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num_heads,
                      const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,

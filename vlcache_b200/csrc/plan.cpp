@@ -26,6 +26,9 @@ namespace {
 
 constexpr int kBlockN = 128;  // keys per K/V tile in the kernel
 constexpr int kTileRows = 128;
+// Parts per split tile: the merge folds a row's parts with 4 lane groups, 4 parts
+// each in flight at once, so up to 16 parts cost one round of loads.
+constexpr int kMaxParts = 16;
 
 struct Tile {
   int seq, kv_head, q_begin, q_count, kpos0, n_kb, kv_len, k_base;
@@ -54,6 +57,9 @@ int validate(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_hea
 
 void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_kv_heads, int T,
                  std::vector<Tile>& tiles) {
+  size_t count = 0;
+  for (int b = 0; b < num_seqs; ++b) count += (size_t)((cu_q[b + 1] - cu_q[b] + T - 1) / T) * num_kv_heads;
+  tiles.reserve(count);
   for (int b = 0; b < num_seqs; ++b) {
     const int ql = cu_q[b + 1] - cu_q[b];
     const int kl = cu_k[b + 1] - cu_k[b];
@@ -112,6 +118,7 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
     int a, b;  // tile indices, b = -1 for a single tile
   };
   std::vector<Pair> pairs;
+  pairs.reserve(tiles.size());
   for (size_t i = 0; i < tiles.size();) {
     size_t e = i;
     while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head) ++e;
@@ -128,24 +135,104 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
     i = e;
   }
 
-  // Time model, in key-block steps: a step of a paired unit costs a little more
-  // than a single-tile step (the two tiles' softmaxes share the SM), each unit
-  // pays a fixed start/epilogue cost, each split part a partial write and its
-  // share of the merge.
-  const double kUnitOverhead = 2.0, kPartOverhead = 0.3, kPairStep = 0.33;
+  // Time model, in single-tile key-block steps (measured on B200: a step of a
+  // paired unit costs about 1.2 steps, each unit about 1.5 steps of start, drain and
+  // epilogue; a split part adds a partial write and its share of the merge).
+  const double kUnitOverhead = 1.5, kPartOverhead = 0.1, kPairStep = 0.2;
   auto pair_cost = [&](const Pair& pr, int kb0, int kb1) {
     const int nb = pr.b >= 0 ? std::max(0, std::min(kb1, tiles[pr.b].n_kb) - kb0) : 0;
     return (kb1 - kb0) + kPairStep * nb + kUnitOverhead;
   };
-  double total_time = 0.0;
-  for (const Pair& pr : pairs) total_time += pair_cost(pr, 0, tiles[pr.a].n_kb);
-  const double avg = total_time / std::max(1, num_sms);
-  // Split units well above the per-SM average into parts of about the average:
-  // every part writes a 32 KB partial per tile that the merge reads back, so the
-  // split count trades balance against merge traffic.
-  const double split_above = std::max(3.0, 1.5 * avg);
-  const double target = std::max(2.0, 1.2 * avg / (1.0 + kPairStep));
+  // Parts of a pair for a target unit cost M: the fewest equal parts whose cost
+  // stays within M (a part of one block when M is below that).
+  auto parts_for = [&](const Pair& pr, double M) {
+    const int n = tiles[pr.a].n_kb;
+    if (pair_cost(pr, 0, n) <= M) return 1;
+    const double per_block = pr.b >= 0 ? 1.0 + kPairStep : 1.0;
+    const double room = M - kUnitOverhead - kPartOverhead;
+    const int np = room >= per_block ? (int)std::ceil(n * per_block / room) : n;
+    return std::max(1, std::min(std::min(np, n), kMaxParts));
+  };
+  auto part_costs = [&](const Pair& pr, int np, std::vector<double>& out) {
+    const int n = tiles[pr.a].n_kb;
+    for (int i = 0; i < np; ++i) {
+      const int kb0 = (int)((int64_t)n * i / np), kb1 = (int)((int64_t)n * (i + 1) / np);
+      out.push_back(pair_cost(pr, kb0, kb1) + (np > 1 ? kPartOverhead : 0.0));
+    }
+  };
+  // Longest-processing-time-first makespan of a set of unit costs on num_sms CTAs.
+  auto lpt_makespan = [&](std::vector<double>& costs) {
+    if ((int)costs.size() <= num_sms) return costs.empty() ? 0.0 : *std::max_element(costs.begin(), costs.end());
+    std::sort(costs.begin(), costs.end(), std::greater<double>());
+    std::priority_queue<double, std::vector<double>, std::greater<double>> heap;
+    for (int c = 0; c < num_sms; ++c) heap.push(0.0);
+    double mk = 0.0;
+    for (double c : costs) {
+      const double l = heap.top() + c;
+      heap.pop();
+      heap.push(l);
+      mk = std::max(mk, l);
+    }
+    return mk;
+  };
+  // Choose the target M among candidates between the cheapest possible part and
+  // the longest unsplit pair by the packed makespan; any split also costs the
+  // merge launch (about two steps on the critical path).
+  const double kMergeLaunch = 2.0;
+  double max_pair = 0.0, total_unsplit = 0.0;
+  for (const Pair& pr : pairs) {
+    const double c = pair_cost(pr, 0, tiles[pr.a].n_kb);
+    max_pair = std::max(max_pair, c);
+    total_unsplit += c;
+  }
+  double best_M = max_pair;
+  const double m_min = kUnitOverhead + kPartOverhead + 1.0 + kPairStep;  // a one-block part
+  if (total_unsplit / std::max(1, num_sms) < max_pair) {
+    // Mean CTA load after splitting every pair to M (decreasing in M).
+    auto mean_load = [&](double M) {
+      double tot = 0.0;
+      for (const Pair& pr : pairs) {
+        const int np = parts_for(pr, M);
+        const int nb_full = pr.b >= 0 ? tiles[pr.b].n_kb : 0;
+        tot += tiles[pr.a].n_kb + kPairStep * nb_full + np * kUnitOverhead + (np > 1 ? np * kPartOverhead : 0.0);
+      }
+      return tot / std::max(1, num_sms);
+    };
+    // M* where the largest unit meets the mean load, then the packed makespan
+    // (LPT) of targets around it decides.
+    double lo = m_min, hi = max_pair;
+    for (int it = 0; it < 16; ++it) {
+      const double mid = 0.5 * (lo + hi);
+      if (mid < mean_load(mid))
+        lo = mid;
+      else
+        hi = mid;
+    }
+    std::vector<double> costs;
+    double best_score = 1e300;
+    auto consider = [&](double M) {
+      costs.clear();
+      bool split = false;
+      for (const Pair& pr : pairs) {
+        const int np = parts_for(pr, M);
+        split |= np > 1;
+        part_costs(pr, np, costs);
+      }
+      const double sc = lpt_makespan(costs) + (split ? kMergeLaunch : 0.0);
+      if (sc < best_score - 1e-9) {
+        best_score = sc;
+        best_M = M;
+      }
+    };
+    consider(max_pair);
+    static const double kScan[] = {0.8, 0.85, 0.9, 0.95, 1.0, 1.05, 1.1, 1.15, 1.2, 1.3, 1.4, 1.6, 2.0};
+    for (double f : kScan) {
+      const double M = hi * f;
+      if (M >= m_min && M < max_pair) consider(M);
+    }
+  }
   std::vector<UnitRec> units;
+  units.reserve(pairs.size() + 64);
   std::vector<std::array<int32_t, kMergeInts>> merges;
   int num_parts = 0;
   auto add_merge = [&](const Tile& t, int part0, int np) {
@@ -164,8 +251,7 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   for (const Pair& pr : pairs) {
     const Tile& ta = tiles[pr.a];
     const int n = ta.n_kb;
-    int np = pair_cost(pr, 0, n) > split_above ? (int)std::ceil(n / target) : 1;
-    np = std::max(1, std::min(np, n));
+    const int np = parts_for(pr, best_M);
     std::vector<int> cuts(np + 1);
     for (int i = 0; i <= np; ++i) cuts[i] = (int)((int64_t)n * i / np);
     // Parts of tile A: all np; parts of tile B: those that start before its end.
@@ -213,21 +299,34 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
 
   const int num_units = (int)units.size();
   const int grid = std::min(num_sms, num_units);
-  // Longest-processing-time-first bin packing onto `grid` persistent CTAs.
-  std::vector<int> order(num_units);
-  for (int i = 0; i < num_units; ++i) order[i] = i;
-  std::stable_sort(order.begin(), order.end(),
-                   [&](int a, int b) { return units[a].cost > units[b].cost; });
-  std::vector<std::vector<int>> per_cta(std::max(grid, 0));
-  typedef std::pair<double, int> Load;
-  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-  for (int c = 0; c < grid; ++c) heap.push(Load(0.0, c));
-  for (int idx : order) {
-    Load l = heap.top();
-    heap.pop();
-    per_cta[l.second].push_back(idx);
-    l.first += units[idx].cost;
-    heap.push(l);
+  // Longest-processing-time-first bin packing onto `grid` persistent CTAs (ties in
+  // unit order); each CTA runs its units longest first.
+  std::vector<std::pair<double, int>> order(num_units);
+  for (int i = 0; i < num_units; ++i) order[i] = std::make_pair(-units[i].cost, i);
+  std::sort(order.begin(), order.end());
+  std::vector<int> cta_of(num_units);
+  {
+    typedef std::pair<double, int> Load;
+    std::vector<Load> heap_store;
+    heap_store.reserve(grid);
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap(std::greater<Load>(),
+                                                                         std::move(heap_store));
+    for (int c = 0; c < grid; ++c) heap.push(Load(0.0, c));
+    for (const auto& o : order) {
+      Load l = heap.top();
+      heap.pop();
+      cta_of[o.second] = l.second;
+      l.first -= o.first;
+      heap.push(l);
+    }
+  }
+  // Units grouped by CTA (counting sort, LPT order inside a CTA).
+  std::vector<int> cta_begin(grid + 1, 0), by_cta(num_units);
+  for (int i = 0; i < num_units; ++i) ++cta_begin[cta_of[i] + 1];
+  for (int c = 0; c < grid; ++c) cta_begin[c + 1] += cta_begin[c];
+  {
+    std::vector<int> fill(cta_begin.begin(), cta_begin.end() - 1);
+    for (const auto& o : order) by_cta[fill[cta_of[o.second]]++] = o.second;
   }
 
   const int64_t off_cta = kPlanHeaderInts;
@@ -265,15 +364,11 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   h[kPOffMergeBlocks] = (int32_t)off_mblocks;
   int32_t* cta = h + off_cta;
   int32_t* up = h + off_units;
-  int pos = 0;
-  for (int c = 0; c < grid; ++c) {
-    cta[c] = pos;
-    for (int idx : per_cta[c]) {
-      for (int k = 0; k < kUnitInts; ++k) up[(int64_t)pos * kUnitInts + k] = units[idx].f[k];
-      ++pos;
-    }
+  for (int c = 0; c <= grid; ++c) cta[c] = cta_begin[c];
+  for (int pos = 0; pos < num_units; ++pos) {
+    const UnitRec& u = units[by_cta[pos]];
+    for (int k = 0; k < kUnitInts; ++k) up[(int64_t)pos * kUnitInts + k] = u.f[k];
   }
-  cta[grid] = pos;
   int32_t* mp = h + off_merges;
   for (size_t i = 0; i < merges.size(); ++i)
     for (int k = 0; k < kMergeInts; ++k) mp[i * kMergeInts + k] = merges[i][k];

@@ -96,6 +96,10 @@ struct Params {
   int64_t num_slots;
   CUtensorMap tm_o;   // out:    dims {HD, num_heads, total_q}, box {64, G, T}
   CUtensorMap tm_p;   // part_o: dims {HD, num_parts * BM},   box {64, BM}
+  // Same tensors, 128-byte swizzle, box {64, G, T} / {64, BM}: the last epilogue of a
+  // tile stores straight from the tile's Q slot (same layout as the Q load).
+  CUtensorMap tm_o128;
+  CUtensorMap tm_p128;
   int tokens_per_tile;  // T
   __nv_bfloat16* out;
   int64_t out_token_stride;
@@ -244,7 +248,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
   }
-  if (warp == 10 && lane == 0) tma_prefetch_desc(&p.tm_q);
+  if (warp == 10 && lane == 0) {
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_o128);
+    tma_prefetch_desc(&p.tm_p128);
+  }
   // Rows beyond T*G of the Q slots are never written by TMA: zero them once so
   // the unused accumulator rows stay finite.
   for (int i = threadIdx.x; i < QSLOTS * BM; i += NUM_THREADS) {
@@ -270,12 +278,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   if (warp == 10) {
     // ------------------------------------------------------------ Q producer
     if (lane == 0) {
+      // The plan is never written by the kernel launched just before (only q/k/v
+      // are): the first unit's fields load while the wait runs.
+      int g = 0, ntile = 0, q_a = 0, q_b = 0;
+      auto fetch = [&](int ui) {
+        const int32_t* u = p.units + (int64_t)ui * kUnitInts;
+        g = u[kUKvHead];
+        ntile = u[kUQCountB] > 0 ? 2 : 1;
+        q_a = u[kUQBeginA];
+        q_b = u[kUQBeginB];
+      };
+      if (u_begin < u_end) fetch(u_begin);
       pdl_wait();  // Q may be written by the preceding kernel
       int load = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
-        const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-        const int g = u[kUKvHead];
-        const int ntile = u[kUQCountB] > 0 ? 2 : 1;
+        if (ui != u_begin) fetch(ui);
         bool ok = true;
         for (int x = 0; x < ntile; ++x, ++load) {
           const int slot = load % QSLOTS;
@@ -284,7 +301,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
             ok = false;
             break;
           }
-          const int q_begin = u[x == 0 ? kUQBeginA : kUQBeginB];
+          const int q_begin = x == 0 ? q_a : q_b;
           uint8_t* qdst = smem + OFF_Q + slot * TILE_BYTES;
           mbar_expect_tx(bars.q_full + slot, 2 * p.rows * 128);
           tma_load_3d(qdst, &p.tm_q, bars.q_full + slot, 0, g * p.group, q_begin);
@@ -296,17 +313,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   } else if (warp == 8) {
     // ------------------------------------------------------------ K/V producer
     if (lane == 0) {
+      // Plan and block tables are never written by the kernel launched just before:
+      // the first unit's fields and its first page are read while the wait runs.
+      int g = 0, kb0 = 0, kb1 = 0, slot0 = 0;
+      const int32_t* u = nullptr;
+      auto fetch = [&](int ui) {
+        u = p.units + (int64_t)ui * kUnitInts;
+        g = u[kUKvHead];
+        kb0 = u[kUKbBegin];
+        kb1 = u[kUKbEnd];
+        slot0 = kb0 < kb1 ? key_block_slot(p, u, kb0) : 0;
+      };
+      if (u_begin < u_end) fetch(u_begin);
       pdl_wait();  // K/V rows are written by the preceding store_kvcache
       int it = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
-        const int32_t* u = p.units + (int64_t)ui * kUnitInts;
-        const int g = u[kUKvHead];
-        const int kb0 = u[kUKbBegin], kb1 = u[kUKbEnd];
+        if (ui != u_begin) fetch(ui);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          const int slot = key_block_slot(p, u, kb);
+          const int slot = kb == kb0 ? slot0 : key_block_slot(p, u, kb);
           if (it >= STAGES && !wait_or_abort(bars.k_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 2, abort_flag)) {
             ok = false;
             break;
@@ -447,11 +474,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
     const uint32_t o_addr = tmem_base + lane_off + TMEM_O + x * 128;
     int t = 0;      // blocks of this tile processed (s_full / p_lo / p_hi phases)
     int nunit = 0;  // units of this tile finished (o_done phases)
+    int qload = 0;  // Q loads of this CTA so far (the Q producer's order)
     for (int ui = u_begin; ui < u_end; ++ui) {
       const int32_t* u = p.units + (int64_t)ui * kUnitInts;
       const UnitView uv = unit_view(u);
       const int n = x == 0 ? uv.n_a : uv.n_b;
+      const int my_load = qload + x;
+      qload += u[kUQCountB] > 0 ? 2 : 1;
       if (n == 0) continue;
+      // The tile's Q slot is free for the epilogue when fewer than QSLOTS loads follow
+      // this tile's (no later Q lands in it).
+      int after = qload - 1 - my_load;
+      for (int uj = ui + 1; uj < u_end && after < QSLOTS; ++uj)
+        after += p.units[(int64_t)uj * kUnitInts + kUQCountB] > 0 ? 2 : 1;
+      const bool own_slot = after < QSLOTS;
       const int g = u[kUKvHead];
       const int kb0 = u[kUKbBegin];
       const int kv_len = u[kUKvLen];
@@ -596,7 +632,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 #pragma unroll
       for (int c = 0; c < 64; ++c)
         orr[c] = pack_bf16x2(__uint_as_float(orr[2 * c]) * inv, __uint_as_float(orr[2 * c + 1]) * inv);
-      if (part >= 0 || q_count == p.tokens_per_tile) {
+      if (own_slot && (part >= 0 || q_count == p.tokens_per_tile)) {
+        // Full tile or split partial, Q slot free: the whole tile goes into the slot
+        // in the Q load's layout (128-byte swizzle: 16-byte chunk c of row r of a
+        // 64-column half at chunk c ^ (r % 8)) and leaves with two TMA stores.  The
+        // slot's last reader, this tile's final Q K^T, completed before o_done.
+        uint8_t* qs = smem + OFF_Q + (my_load % QSLOTS) * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          *reinterpret_cast<uint4*>(qs + (k >> 3) * HALF_BYTES + row * 128 + (((k & 7) ^ (row & 7)) << 4)) =
+              make_uint4(orr[4 * k], orr[4 * k + 1], orr[4 * k + 2], orr[4 * k + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1 + x, kTileThreads);
+        if (row == 0) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (part < 0)
+              tma_store_3d(&p.tm_o128, qs + h * HALF_BYTES, 64 * h, g * p.group, q_begin);
+            else
+              tma_store_2d(&p.tm_p128, qs + h * HALF_BYTES, 64 * h, part * BM);
+          }
+          bulk_commit_group();
+        }
+      } else if (part >= 0 || q_count == p.tokens_per_tile) {
         // Full tile or split partial: stage 32 columns at a time in shared memory,
         // alternating two buffers (64-byte swizzle: 16-byte chunk c of row r at chunk
         // c ^ ((r / 2) % 4)), and let one thread write each with a TMA tensor store.
@@ -650,9 +708,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 // 256-thread blocks listed by the planner as (merge, first row).  A warp is 4
 // groups of 8 lanes; lane c of a group owns dims [16 c, 16 c + 16) (one 32-byte
 // load per part).  With R rows per warp (4, 2 or 1) each row has K = 4 / R groups,
-// group k folding parts k, k + K, ... with a running max (a part's loads do not
-// depend on the running state, so consecutive parts are in flight together); the
-// K states of a row combine through shuffles.
+// group k folding parts k, k + K, ... with a running max, kMergeBatch parts per
+// round with their loads in flight together; the K states of a row combine
+// through shuffles.
+constexpr int kMergeBatch = 4;
 __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __restrict__ merges,
                                                                const int32_t* __restrict__ blocks,
                                                                const __nv_bfloat16* __restrict__ part_o,
@@ -661,10 +720,10 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
                                                                int64_t out_token_stride) {
   const int entry = __ldg(blocks + blockIdx.x);
   const int32_t* m = merges + (int64_t)(entry >> 8) * kMergeInts;
-  pdl_wait();  // the partials are written by the attention kernel launched just before
   const int q_begin = __ldg(m + kMQBegin), g = __ldg(m + kMKvHead);
   const int part0 = __ldg(m + kMPartBegin), nparts = __ldg(m + kMNumParts);
   const int R = __ldg(m + kMRowsPerWarp), nrows = __ldg(m + kMRows);
+  pdl_wait();  // the partials are written by the attention kernel launched just before
   const int K = 4 / R;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = lane >> 3, c = lane & 7;
@@ -677,24 +736,45 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
   float m_run = -INFINITY, L = 0.f;
   if (active) {
-#pragma unroll 4
-    for (int i = k0; i < nparts; i += K) {
-      const int64_t pr = (int64_t)(part0 + i) * BM + row;
-      const float2 v = __ldg(&ml[pr]);
-      const uint4* src = reinterpret_cast<const uint4*>(part_o + pr * HD) + 2 * c;
-      const uint4 r0 = __ldg(src), r1 = __ldg(src + 1);
-      const float m_new = fmaxf(m_run, v.x);
-      const float mr = m_new == -INFINITY ? 0.f : m_new;
-      const float a = fast_exp2(m_run - mr);      // 0 while nothing is accumulated
-      const float w = fast_exp2(v.x - mr) * v.y;  // weight of O_p / l_p (0 for an empty part)
-      m_run = m_new;
-      L = fmaf(L, a, w);
-      const uint32_t wds[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+    // Batches of kMergeBatch parts: all loads of a batch are issued before any of
+    // them is used, then the batch is folded with one rescale of the accumulator.
+    for (int i0 = k0; i0 < nparts; i0 += kMergeBatch * K) {
+      float2 v[kMergeBatch];
+      uint4 r0[kMergeBatch], r1[kMergeBatch];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wds[k]));
-        acc[2 * k] = fmaf(w, o.x, acc[2 * k] * a);
-        acc[2 * k + 1] = fmaf(w, o.y, acc[2 * k + 1] * a);
+      for (int s = 0; s < kMergeBatch; ++s) {
+        const int i = i0 + s * K;
+        if (i < nparts) {
+          const int64_t pr = (int64_t)(part0 + i) * BM + row;
+          const uint4* src = reinterpret_cast<const uint4*>(part_o + pr * HD) + 2 * c;
+          v[s] = __ldg(&ml[pr]);
+          r0[s] = __ldg(src);
+          r1[s] = __ldg(src + 1);
+        } else {
+          v[s] = make_float2(-INFINITY, 0.f);  // weight 0
+          r0[s] = r1[s] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      float m_new = m_run;
+#pragma unroll
+      for (int s = 0; s < kMergeBatch; ++s) m_new = fmaxf(m_new, v[s].x);
+      const float mr = m_new == -INFINITY ? 0.f : m_new;
+      const float a = fast_exp2(m_run - mr);  // 0 while nothing is accumulated
+      m_run = m_new;
+      L *= a;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc[k] *= a;
+#pragma unroll
+      for (int s = 0; s < kMergeBatch; ++s) {
+        const float w = fast_exp2(v[s].x - mr) * v[s].y;  // weight of O_p / l_p (0 for an empty part)
+        L += w;
+        const uint32_t wds[8] = {r0[s].x, r0[s].y, r0[s].z, r0[s].w, r1[s].x, r1[s].y, r1[s].z, r1[s].w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float2 o = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wds[k]));
+          acc[2 * k] = fmaf(w, o.x, acc[2 * k]);
+          acc[2 * k + 1] = fmaf(w, o.y, acc[2 * k + 1]);
+        }
       }
     }
   }
@@ -795,6 +875,8 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)out_token_stride * 2};
     const uint32_t box[3] = {32, (uint32_t)group, (uint32_t)T};
     if (encode_tmap_bf16(&prm.tm_o, out, 3, dims, strides, box, 64) != VLC_OK) return VLC_ERR_CUDA;
+    const uint32_t box128[3] = {64, (uint32_t)group, (uint32_t)T};
+    if (encode_tmap_bf16(&prm.tm_o128, out, 3, dims, strides, box128, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   prm.cta_offsets = plan_dev + plan_host[kPOffCta];
   prm.units = plan_dev + plan_host[kPOffUnits];
@@ -817,8 +899,11 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     const uint64_t strides[1] = {(uint64_t)HD * 2};
     const uint32_t box[2] = {32, (uint32_t)BM};
     if (encode_tmap_bf16(&prm.tm_p, prm.part_o, 2, dims, strides, box, 64) != VLC_OK) return VLC_ERR_CUDA;
+    const uint32_t box128[2] = {64, (uint32_t)BM};
+    if (encode_tmap_bf16(&prm.tm_p128, prm.part_o, 2, dims, strides, box128, 128) != VLC_OK) return VLC_ERR_CUDA;
   } else {
     prm.tm_p = prm.tm_o;  // unused
+    prm.tm_p128 = prm.tm_o128;
   }
   prm.tokens_per_tile = T;
 

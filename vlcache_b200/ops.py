@@ -166,6 +166,8 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_t
     Paged: ``k``/``v`` are one layer's ``[num_blocks, block_size, Hk, D]`` caches and
     ``block_tables`` maps sequences to pages.  Contiguous (``block_tables`` None): ``k``/``v``
     are ``[total_k, Hk, D]`` (any token stride) laid out by cu_seqlens_k.
+    The kernel is a programmatic dependent launch of the previous kernel on the
+    stream: that kernel may produce q/k/v, but not the plan or ``block_tables``.
     """
     _require_cuda(q, k, v, block_tables)
     assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
