@@ -26,9 +26,9 @@ namespace {
 
 constexpr int kBlockN = 128;  // keys per K/V tile in the kernel
 constexpr int kTileRows = 128;
-// Parts per split tile: the merge folds a row's parts with 4 lane groups, 4 parts
-// each in flight at once, so up to 16 parts cost one round of loads.
-constexpr int kMaxParts = 16;
+// Parts per split tile: the merge folds a row's parts with 4 lane groups, 5 parts
+// each in flight at once, so up to 20 parts cost one round of loads.
+constexpr int kMaxParts = 20;
 
 struct Tile {
   int seq, kv_head, q_begin, q_count, kpos0, n_kb, kv_len, k_base;

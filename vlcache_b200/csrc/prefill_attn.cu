@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 // group k folding parts k, k + K, ... with a running max, kMergeBatch parts per
 // round with their loads in flight together; the K states of a row combine
 // through shuffles.
-constexpr int kMergeBatch = 4;
+constexpr int kMergeBatch = 5;
 __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __restrict__ merges,
                                                                const int32_t* __restrict__ blocks,
                                                                const __nv_bfloat16* __restrict__ part_o,
