@@ -50,6 +50,7 @@ N_IMG = GRID_H * GRID_W
 R = math.ceil(RATIO * N_IMG)
 SEQLEN = PREFIX + N_IMG + SUFFIX
 BLOCK = 256
+SPEC_BF16_TFLOPS = 2250.0  # B200 dense bf16 spec-sheet peak (for the second fraction)
 OLD_PREFIX = 12            # where the image sat in the request that cached it
 DEC_SEQS, DEC_H, DEC_HK, DEC_LAYERS = 256, 28, 4, 28
 DEC_DISTINCT = 4           # distinct 3.5 GB layer caches cycled through (each >> L2)
@@ -606,6 +607,7 @@ def main():
             "step_us_per_layer": ms_step * 1e3 / LAYERS,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": achieved / tf_peak, "peak_kind": f"bf16 burst ({peak_kind})", "traffic": traffic,
+                         "frac_spec": achieved / SPEC_BF16_TFLOPS,
                          "kernel": "prefill_attn_kernel (+ split merge)",
                          "flop_per_launch": int(flop_step // LAYERS)},
             "decode": {"workload": "cfg5: Qwen2.5-VL-7B, 256 seqs, KV len U[2700,10700], block 256",
