@@ -193,6 +193,36 @@ def test_prefill_full_causal_7b(ops):
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
 
 
+@pytest.mark.parametrize("block_size", [128, 512])
+def test_prefill_block_sizes_and_empty_sequences(ops, block_size):
+    """Pages of 128 and 512 keys; empty virtual sequences (no suffix, no prefix) and keys
+    ending on and off a 128-key boundary."""
+    H, Hk = 16, 2
+    specs = [(0, 640, 0, 64), (7, 121, 0, 121), (20, 500, 12, 0), (3, 250, 5, 40)]
+    case = make_warm_case(specs, H, Hk, device="cuda", seed=8, block_size=block_size)
+    assert any(case.cu_q[i + 1] == case.cu_q[i] for i in range(len(case.cu_q) - 1))
+    ref = oatt.prefill_attention(case.q.cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    out, _ = _run_prefill(ops, case, H, Hk)
+    mx, mean = attn_errors(out, ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
+def test_prefill_long_keys_max_parts(ops):
+    """48 text rows after a 40,000-token image: the long tiles split into the planner's
+    maximum part count (one round of merge loads per lane group)."""
+    H, Hk = 16, 2
+    case = make_warm_case([(20, 40000, 48, 0)], H, Hk, device="cuda", seed=9)
+    out, plan = _run_prefill(ops, case, H, Hk)
+    h = plan.host
+    merges = h[int(h[14]):int(h[14]) + plan.num_merges * 8].reshape(-1, 8)
+    assert int(merges[:, 4].max()) == 20
+    ref = oatt.prefill_attention(case.q.cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    mx, mean = attn_errors(out, ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
 # ------------------------------------------------------------------ decode
 @pytest.mark.parametrize("model,lens", [("7b", [1, 63, 64, 65, 700, 2711, 5000, 10700]),
                                         ("3b", [255, 256, 257, 4097])])
