@@ -58,6 +58,14 @@ int vlc_get_device_error(int reset);
 /* Number of SMs of the current device (used by the planners). */
 int vlc_num_sms(void);
 
+/* Self-test of the bounded waits every kernel uses (no fault, no hang): one warp
+ * waits on a shared-memory barrier that is completed (arrive != 0) or never
+ * completed (arrive == 0).  In the second case the wait gives up after
+ * limit_cycles (1 .. about 4e9) and records VLC_DEV_ERR_TIMEOUT + VLC_SELFTEST_ROLE
+ * in the device error word; the kernel returns and the context stays usable. */
+#define VLC_SELFTEST_ROLE 31
+int vlc_selftest_bounded_wait(long long limit_cycles, int arrive, void* stream);
+
 /* --------------------------------------------------------------------------
  * KV scatter.
  * Replaces nanovllm/layers/attention.py:10-40 (store_kvcache_kernel + store_kvcache):

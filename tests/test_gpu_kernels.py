@@ -67,6 +67,25 @@ def test_store_kvcache_bad_slot_flagged(ops):
     assert torch.equal(kc.view(-1, 256)[0], k[0].reshape(-1))
 
 
+def test_bounded_wait_gives_up_and_context_stays_usable(ops):
+    """Every kernel's barrier waits are bounded: a wait on a barrier nothing completes gives
+    up after the limit (~1 ms here), records TIMEOUT + role, and the next launches run."""
+    import ctypes
+    from vlcache_b200._lib import lib
+    L = lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.vlc_selftest_bounded_wait(2_000_000, 1, stream) == 0     # completed barrier: no error
+    assert ops.device_error(reset=True) == 0
+    assert L.vlc_selftest_bounded_wait(2_000_000, 0, stream) == 0     # never completed: gives up
+    assert ops.device_error(reset=True) == 110 + 31
+    k = torch.randn(4, 2, 128, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(2, 256, 2, 128, dtype=torch.bfloat16, device="cuda")
+    ops.store_kvcache(k, k, kc, torch.zeros_like(kc), torch.tensor([3, 0, 7, 9], dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(kc.view(-1, 256)[3], k[0].reshape(-1))
+
+
 # ------------------------------------------------------------------ M-RoPE shift
 @pytest.mark.parametrize("hk,delta", [(2, (16, 16, 16)), (4, (37, 5, -3))])
 def test_mrope_shift_matches_oracle(ops, hk, delta):

@@ -23,6 +23,7 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_version": (c_int, []),
     "vlc_status_string": (ctypes.c_char_p, [c_int]),
     "vlc_get_device_error": (c_int, [c_int]),
+    "vlc_selftest_bounded_wait": (c_int, [c_i64, c_int, c_vp]),
     "vlc_num_sms": (c_int, []),
     "vlc_store_kvcache": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_i64, c_vp]),
     "vlc_mrope_shift": (c_int, [c_vp, c_vp, c_i64, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_int,

@@ -83,17 +83,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait.  Returns false (and records `code`) when the limit is hit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+// Bounded wait.  Returns false (and records `code`) after `limit_cycles`.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int code, long long limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > VLC_WAIT_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit_cycles) {
       record_error(code);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  return mbar_wait_bounded(bar, parity, code, VLC_WAIT_LIMIT_CYCLES);
 }
 
 // ---------------------------------------------------------------- proxies / fences

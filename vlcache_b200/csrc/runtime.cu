@@ -41,6 +41,29 @@ extern "C" int vlc_get_device_error(int reset) {
   return v;
 }
 
+// Self-test of the bounded mbarrier wait every kernel uses: one warp waits on a
+// barrier that is (arrive != 0) or is not (arrive == 0) completed.  Without the
+// arrival the wait gives up after limit_cycles and records
+// VLC_DEV_ERR_TIMEOUT + VLC_SELFTEST_ROLE; the kernel then returns normally.
+namespace vlc {
+__global__ void bounded_wait_selftest_kernel(long long limit_cycles, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (arrive && threadIdx.x == 0) mbar_arrive(&bar);
+  mbar_wait_bounded(&bar, 0, VLC_DEV_ERR_TIMEOUT + VLC_SELFTEST_ROLE, limit_cycles);
+}
+}  // namespace vlc
+
+extern "C" int vlc_selftest_bounded_wait(long long limit_cycles, int arrive, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > VLC_WAIT_LIMIT_CYCLES) return VLC_ERR_SHAPE;
+  vlc::bounded_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_cycles, arrive);
+  return vlc::launch_status();
+}
+
 extern "C" int vlc_num_sms(void) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
