@@ -5,11 +5,12 @@ Workload (one "step"): one warm request of Qwen2.5-VL-3B shapes (16 q heads, 2 K
 head_dim 128, 36 layers) whose 3840x2160 image (77x137 = 10,549 vision tokens) was seen
 before at another offset; 20 prefix + 48 suffix text tokens; recompute ratio 0.1 (first
 1,055 vision rows).  Per step, exactly what the warm prefill runs on the attention path:
-  * the reused image K/V rows of all 36 layers move to the request's pages with the
-    M-RoPE position shift (vlc_mrope_shift, one launch);
-  * per layer: scatter of the 1,123 recomputed K/V rows (vlc_store_kvcache) and the
-    sparse-query paged prefill attention, 1,123 query rows over 10,617 keys
-    (vlc_prefill_attn + its split merge).
+  * the reused image K/V rows of every layer move to the request's pages with the
+    M-RoPE position shift (vlc_mrope_shift, one launch per layer on a low-priority stream,
+    so that later layers' rows move while earlier layers compute);
+  * per layer: scatter of the 1,123 recomputed K/V rows (vlc_store_kvcache), a wait for
+    that layer's moved rows, and the sparse-query paged prefill attention, 1,123 query
+    rows over 10,617 keys (vlc_prefill_attn + its split merge).
 Inputs are seeded N(0,1) (synthetic: no checkpoint), distinct per layer (≈0.8 GB per
 step, larger than the 126 MB L2, so no flush is needed between steps).
 
@@ -179,6 +180,9 @@ class WarmPrefillWorkload:
         self.ws = torch.empty(max(1, self.plan.workspace_bytes), dtype=torch.uint8, device=device)
         self.scale = 1.0 / math.sqrt(D)
         self.rows_moved = int(self.src.numel())
+        self.kvc = kvc
+        # the re-placement of the reused image rows runs on the lowest-priority stream
+        self.side = torch.cuda.Stream(device=device, priority=0)
 
     def q(self, l):
         return self.qkv[l, :, :H * D].view(self.total_q, H, D)
@@ -194,10 +198,17 @@ class WarmPrefillWorkload:
                                    self.scale, self.out[l], self.ws)
 
     def step(self):
-        self.ops.mrope_shift_all_layers(self.kv_cache, self.src, self.dst, self.delta)
+        # Layer l's reused image rows are re-placed (moved + M-RoPE shifted) on a
+        # low-priority stream while earlier layers compute; layer l waits for its own.
+        ready = self.kvc.copy_image_kv_per_layer(self.kv_cache, self.src, self.dst, self.delta, self.side)
+        cur = torch.cuda.current_stream()
         for l in range(LAYERS):
+            # (the wait precedes the scatter: the attention stays the scatter's direct
+            # successor, so its programmatic launch overlaps the scatter)
+            cur.wait_event(ready[l])
             self.ops.store_kvcache(self.k(l), self.v(l), self.kv_cache[0, l], self.kv_cache[1, l], self.slot_mapping)
             self.attention(l)
+        cur.wait_stream(self.side)
 
     def attention_only(self):
         for l in range(LAYERS):
@@ -205,19 +216,21 @@ class WarmPrefillWorkload:
 
     @property
     def launches_per_step(self):
-        per_layer = 2 + (1 if self.plan.num_merges > 0 else 0)
-        return 1 + LAYERS * per_layer
+        per_layer = 3 + (1 if self.plan.num_merges > 0 else 0)  # shift, scatter, attention (+ merge)
+        return LAYERS * per_layer
 
 
 def graph_of(fn):
-    s = torch.cuda.Stream()
+    """Capture ``fn`` on the highest-priority stream (kernel priorities are kept in the
+    graph, so side-stream work yields SMs to it)."""
+    s = torch.cuda.Stream(priority=torch.cuda.Stream.priority_range()[1])
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         fn()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, stream=s):
         fn()
     torch.cuda.synchronize()
     return g
@@ -292,6 +305,8 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
         cur = torch.cuda.current_stream()
         h2d.wait_stream(cur)
         upload(0)
+        # eager launches: the image rows of all layers move in one launch (the per-layer
+        # variant used by the graphed step costs 36 host launches here)
         wl.ops.mrope_shift_all_layers(wl.kv_cache, wl.src, wl.dst, wl.delta)
         for l in range(LAYERS):
             b = l % 2

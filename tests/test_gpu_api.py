@@ -25,9 +25,11 @@ def api(cuda_lib):
     return ops, kvc, Attention, ctx
 
 
-def test_attention_forward_warm_prefill(api):
+@pytest.mark.parametrize("gated", [False, True])
+def test_attention_forward_warm_prefill(api, gated):
     """Warm request through the drop-in layer: recomputed K/V are scattered by the layer,
-    then the recomputed rows attend over the paged cache (reused image rows included)."""
+    then the recomputed rows attend over the paged cache (reused image rows included).
+    gated: the layer first waits for its Context.kv_ready event (recorded on a side stream)."""
     ops, kvc, Attention, ctx = api
     H, Hk, D = 16, 2, 128
     g = torch.Generator().manual_seed(11)
@@ -55,6 +57,15 @@ def test_attention_forward_warm_prefill(api):
     attn = Attention(H, D, 1 / math.sqrt(D), Hk)
     attn.k_cache, attn.v_cache = k_cache.cuda(), v_cache.cuda()
     builder.upload(batch, device="cuda")
+    if gated:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        ev = torch.cuda.Event()
+        with torch.cuda.stream(side):
+            torch.cuda._sleep(1000)
+            ev.record(side)
+        ctx.get_context().kv_ready = [ev]
+        attn.layer_id = 0
     out = attn(q.cuda(), k.cuda(), v.cuda())
     torch.cuda.synchronize()
     assert torch.equal(attn.k_cache.cpu(), kc_ref) and torch.equal(attn.v_cache.cpu(), vc_ref)
@@ -169,6 +180,29 @@ def test_copy_image_kv_all_layers_with_shift(api):
         untouched = np.setdiff1d(np.arange(NB * 256), new_slots)
         assert np.array_equal(bits(got[0, layer]).reshape(-1, Hk * D)[untouched],
                               bits(kv[0, layer]).reshape(-1, Hk * D)[untouched])
+
+
+def test_copy_image_kv_per_layer_matches_one_launch(api):
+    """The per-layer variant (one launch per layer on a side stream, one event per layer)
+    leaves the cache bit-identical to the all-layers launch."""
+    ops, kvc, Attention, ctx = api
+    L, NB, Hk, D = 3, 10, 2, 128
+    g = torch.Generator().manual_seed(17)
+    kv = torch.randn(2, L, NB, 256, Hk, D, generator=g).to(torch.bfloat16)
+    old_slots, new_slots = kvc.image_reuse_slots(30, 30 + 700, 70, [7, 4, 9, 5], 10, [0, 1, 2, 3])
+    delta = (20, 20, 20)
+    a, b = kv.cuda(), kv.cuda()
+    kvc.copy_image_kv(a, old_slots, new_slots, delta)
+    side = torch.cuda.Stream()
+    src = torch.from_numpy(old_slots).cuda()
+    dst = torch.from_numpy(new_slots).cuda()
+    ready = kvc.copy_image_kv_per_layer(b, src, dst, delta, side)
+    assert len(ready) == L
+    for ev in ready:
+        torch.cuda.current_stream().wait_event(ev)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert ops.device_error() == 0
 
 
 def test_prefill_cfg3_style_batch(api):

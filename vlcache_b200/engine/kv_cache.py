@@ -39,6 +39,7 @@ def allocate_kv_cache(model: torch.nn.Module | None, num_layers: int, num_blocks
             if hasattr(module, "k_cache") and hasattr(module, "v_cache"):
                 module.k_cache = kv_cache[0, layer_id]
                 module.v_cache = kv_cache[1, layer_id]
+                module.layer_id = layer_id  # index into Context.kv_ready
                 layer_id += 1
     return kv_cache
 
@@ -74,6 +75,32 @@ def copy_image_kv(kv_cache: torch.Tensor, old_slots, new_slots, delta_thw=(0, 0,
     src = torch.as_tensor(np.asarray(old_slots, dtype=np.int32)).pin_memory().to(dev, non_blocking=True)
     dst = torch.as_tensor(np.asarray(new_slots, dtype=np.int32)).pin_memory().to(dev, non_blocking=True)
     (shift or MRopeShift()).shift_all_layers(kv_cache, src, dst, delta_thw)
+
+
+def copy_image_kv_per_layer(kv_cache: torch.Tensor, src_slots: torch.Tensor, dst_slots: torch.Tensor,
+                            delta_thw=(0, 0, 0), stream: torch.cuda.Stream | None = None,
+                            shift: MRopeShift | None = None) -> list:
+    """``copy_image_kv`` as one launch per layer on ``stream`` (device int32 slot tensors),
+    returning one CUDA event per layer.  Pass the events as ``set_context(..., kv_ready=...)``:
+    each attention layer waits only for its own layer's rows, so the re-placement of later
+    layers overlaps the compute of earlier ones.  Give ``stream`` a lower priority than
+    the compute stream (the layers' kernels then take the SMs first)."""
+    sh = shift or MRopeShift()
+    cur = torch.cuda.current_stream()
+    stream = stream or cur
+    stream.wait_stream(cur)
+    events = []
+    with torch.cuda.stream(stream):
+        for layer in range(kv_cache.shape[1]):
+            if src_slots.numel():
+                sh.shift_layer(kv_cache[0, layer], kv_cache[1, layer], src_slots, dst_slots, delta_thw)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            events.append(ev)
+    if stream is not cur:
+        src_slots.record_stream(stream)
+        dst_slots.record_stream(stream)
+    return events
 
 
 @dataclass

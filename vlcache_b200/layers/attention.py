@@ -61,10 +61,16 @@ class Attention(nn.Module):
         self.scale = scale
         self.num_kv_heads = num_kv_heads
         self.k_cache = self.v_cache = torch.tensor([])
+        self.layer_id = None  # set by engine.kv_cache.allocate_kv_cache (or the caller)
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
+        if context.kv_ready is not None:    # this layer's reused rows are placed
+            # (waited before the scatter: the attention kernel stays the scatter's direct
+            # successor in the stream, so its programmatic launch overlaps the scatter)
+            assert self.layer_id is not None, "kv_ready needs Attention.layer_id"
+            torch.cuda.current_stream().wait_event(context.kv_ready[self.layer_id])
         if k_cache.numel() and v_cache.numel():
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if context.is_prefill:

@@ -10,7 +10,9 @@ keep working):
                           built without a device-to-host read;
   * ``max_context_len`` — host-side bound for the decode grid (defaults to the
                           block-table width times the block size: no device read);
-  * ``workspace``       — scratch tensor reused by every layer of the step.
+  * ``workspace``       — scratch tensor reused by every layer of the step;
+  * ``kv_ready``        — per-layer CUDA events (``engine.kv_cache.copy_image_kv_per_layer``):
+                          layer i's attention waits for event i before it reads the cache.
 """
 from __future__ import annotations
 
@@ -36,6 +38,7 @@ class Context:
     cu_seqlens_k_host: Any = None
     max_context_len: int | None = None
     workspace: torch.Tensor | None = None
+    kv_ready: Any = None
 
 
 _CONTEXT = Context()
@@ -47,11 +50,12 @@ def get_context() -> Context:
 
 def set_context(is_prefill, cu_seqlens_q=None, cu_seqlens_k=None, max_seqlen_q=0, max_seqlen_k=0,
                 slot_mapping=None, context_lens=None, block_tables=None, *, prefill_plan=None,
-                cu_seqlens_q_host=None, cu_seqlens_k_host=None, max_context_len=None, workspace=None):
+                cu_seqlens_q_host=None, cu_seqlens_k_host=None, max_context_len=None, workspace=None,
+                kv_ready=None):
     global _CONTEXT
     _CONTEXT = Context(is_prefill, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, slot_mapping,
                        context_lens, block_tables, prefill_plan, cu_seqlens_q_host, cu_seqlens_k_host,
-                       max_context_len, workspace)
+                       max_context_len, workspace, kv_ready)
 
 
 def reset_context():
