@@ -37,15 +37,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n\t.reg .pred P;\n\t"
-      "elect.sync _|P, 0xffffffff;\n\t"
-      "selp.b32 %0, 1, 0, P;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
 
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -95,9 +86,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
   }
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
-  return mbar_wait_bounded(bar, parity, code, VLC_WAIT_LIMIT_CYCLES);
-}
 
 // ---------------------------------------------------------------- proxies / fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -116,13 +104,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_t* bar, int x, int y,
                                             int z) {
@@ -147,9 +128,8 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// The smem sources of this thread's committed bulk stores have been read (all, or all
-// but the most recent group).
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The shared-memory sources of this thread's committed bulk stores, all but the most
+// recent group, have been read.
 __device__ __forceinline__ void bulk_wait_read_allbut1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // This thread's committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -182,32 +162,15 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T   (kind::f16, bf16 inputs, fp32 accumulate)
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
-// D[tmem] (+)= A[tmem] * B[smem]^T  (A: M rows on TMEM lanes, K packed two bf16 per column)
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                        uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// The same issues with each smem descriptor given as its two 32-bit words, so a
-// caller stepping through K only adds to the low word (start address field) of a
-// precomputed descriptor.  No memory clobber: ordering against the producers is
-// through mbarrier waits (volatile asm keeps program order among these).
+// tcgen05.mma kind::f16 (bf16 inputs, fp32 accumulate), single CTA:
+//   umma_ss_w: D[tmem] (+)= A[smem] * B[smem]^T
+//   umma_ts_w: D[tmem] (+)= A[tmem] * B[smem]^T  (A: M rows on TMEM lanes, K packed two
+//              bf16 per column)
+// Each smem descriptor is given as its two 32-bit words, so a caller stepping through
+// K only adds to the low word (start address field) of a precomputed descriptor.  No
+// memory clobber: ordering against the producers is through mbarrier waits (volatile
+// asm keeps program order among these).
 __device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
                                           uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -268,18 +231,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -291,26 +242,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+
 // ---------------------------------------------------------------- UMMA descriptors
 // Shared-memory matrix descriptor for the 128-byte swizzle canonical layouts
-// (tcgen05 "version 1" descriptor).  Addresses/offsets are in bytes.
+// (tcgen05 "version 1" descriptor), kept as its two 32-bit words:
+//   low : start address >> 4 (bits 0-13), leading byte offset >> 4 (bits 16-29);
+//   high: stride byte offset >> 4 (bits 0-13), version 1 (bit 14), SWIZZLE_128B (2 << 29).
 //   K-major : rows of 128 B (64 bf16 along K), 8-row groups `sbo` apart.
 //   MN-major: rows of 128 B (64 bf16 along M/N) one per K index, 8-row K groups
 //             `sbo` apart, successive 64-element M/N blocks `lbo` apart.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo,
-                                                    uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
-  return d;
-}
-
-// The two words of umma_desc_sw128.  Shared-memory addresses are below 2^18, so
-// adding (byte offset >> 4) to the low word never carries out of the 14-bit
-// start-address field.
+// Shared-memory addresses are below 2^18, so adding (byte offset >> 4) to the low
+// word never carries out of the 14-bit start-address field.
 __host__ __device__ constexpr uint32_t umma_desc_sw128_hi(uint32_t sbo) {
   return ((sbo >> 4) & 0x3FFF) | (1u << 14) | (2u << 29);
 }
@@ -375,36 +317,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x on the FMA pipe (offloads the special-function unit).  x = n + r with n the
-// nearest integer (added to 1.5 * 2^23 so n lands in the low mantissa bits) and
-// r in [-0.5, 0.5]; 2^r by a degree-3 polynomial fitted here for minimum relative
-// error (max 7.5e-5, far below bf16's 2^-9); 2^n by adding n to the exponent
-// field.  x is clamped at -125, so masked (-inf) inputs give ~2.4e-38, not 0.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;
-  const float r = x - (t - 12582912.0f);
-  const float p = fmaf(fmaf(fmaf(0.05517166853f, r, 0.24261114001f), r, 0.69326096773f), r, 0.99992805719f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
 
-// exp2_fma on a pair, the float arithmetic as packed f32x2 operations.
-__device__ __forceinline__ void exp2_fma2(uint64_t x2, float& e0, float& e1) {
-  float x0, x1;
-  f2_unpack(x2, x0, x1);
-  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t t = f2_add(xc, magic);
-  const uint64_t n = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));
-  const uint64_t r = f2_fma(n, f2_pack(-1.0f, -1.0f), xc);
-  uint64_t p = f2_fma(f2_pack(0.05517166853f, 0.05517166853f), r, f2_pack(0.24261114001f, 0.24261114001f));
-  p = f2_fma(p, r, f2_pack(0.69326096773f, 0.69326096773f));
-  p = f2_fma(p, r, f2_pack(0.99992805719f, 0.99992805719f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
 
 }  // namespace vlc

@@ -77,9 +77,6 @@ constexpr uint32_t IDESC_QK = umma_idesc_bf16(128, 128, false, false);
 constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, 128, false, true);
 
 constexpr int kTileThreads = 128;  // softmax threads per tile
-// Of every 4 key pairs of P, how many take exp2 on the FMA pipe (exp2_fma) instead
-// of the special-function unit; the rest use ex2.approx.
-constexpr int kFmaExpPairsOf4 = 0;
 
 struct Params {
   CUtensorMap tm_q;   // dims {HD, num_heads, total_q}, box {64, G, T}
@@ -570,15 +567,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
               const uint64_t x2 =
                   f2_fma(f2_pack(__uint_as_float(sr[base + 2 * c]), __uint_as_float(sr[base + 2 * c + 1])), scale2,
                          negm2);
-              float e0, e1;
-              if ((c & 3) >= 4 - kFmaExpPairsOf4) {
-                exp2_fma2(x2, e0, e1);
-              } else {
-                float x0, x1;
-                f2_unpack(x2, x0, x1);
-                e0 = fast_exp2(x0);
-                e1 = fast_exp2(x1);
-              }
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
               lsum = f2_add(lsum, f2_pack(e0, e1));
               sr[base + c] = pack_bf16x2(e0, e1);
             }
