@@ -299,6 +299,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
             break;
           }
           const int q_begin = x == 0 ? q_a : q_b;
+          // At launch every CTA loads at once and HBM is the limit: the first tile's Q
+          // (an operand of the first Q K^T) lands before the second tile's is requested.
+          if (load == 1 && !wait_or_abort(bars.q_full + 0, 0u, VLC_DEV_ERR_TIMEOUT + 1, abort_flag)) {
+            ok = false;
+            break;
+          }
           uint8_t* qdst = smem + OFF_Q + slot * TILE_BYTES;
           mbar_expect_tx(bars.q_full + slot, 2 * p.rows * 128);
           tma_load_3d(qdst, &p.tm_q, bars.q_full + slot, 0, g * p.group, q_begin);
@@ -340,6 +346,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           tma_load_3d(kdst, &p.tm_k, bars.k_full + s, 0, g, slot);
           tma_load_3d(kdst + HALF_BYTES, &p.tm_k, bars.k_full + s, 64, g, slot);
           if (it >= STAGES && !wait_or_abort(bars.v_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 3, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // Likewise the first K block lands before V and the next blocks are requested.
+          if (it == 0 && !wait_or_abort(bars.k_full + 0, 0u, VLC_DEV_ERR_TIMEOUT + 3, abort_flag)) {
             ok = false;
             break;
           }
