@@ -337,17 +337,8 @@ def metadata_bench(device, reps: int = 20):
     slots): the vectorised host builder vs the device builder (descriptor upload + one
     kernel), wall time per batch, median of ``reps``."""
     from vlcache_b200.engine import kv_cache as kvc
-    rng = np.random.default_rng(3)
-    n_img = 39 * 69
-    R3 = kvc.recompute_count(0.05, n_img)
-    reqs, reuse, page = [], [], 0
-    for i in range(64):
-        pre, suf = int(rng.integers(0, 513)), int(rng.integers(16, 129))
-        n = pre + n_img + suf
-        nb = (n + BLOCK - 1) // BLOCK
-        reqs.append(kvc.WarmRequest(n, list(range(page, page + nb)), pre, pre + n_img, R3, True))
-        page += nb
-        reuse.append(kvc.ImageReuse(i, 5, list(range(100000, 100000 + 12))))
+    reqs, _, n_img, R3 = cfg3_requests()
+    reuse = [kvc.ImageReuse(i, 5, list(range(100000, 100000 + 12))) for i in range(len(reqs))]
     builder = kvc.WarmPrefillBuilder(H, HK)
 
     def host():
@@ -375,6 +366,55 @@ def metadata_bench(device, reps: int = 20):
     q_rows = int(builder.build(reqs).cu_seqlens_q[-1])
     return {"workload": f"cfg3: 64 warm requests, {q_rows} query rows, "
                         f"{64 * (n_img - R3)} reused image rows", **out}
+
+
+def cfg3_requests():
+    """64 warm requests sharing a 1920x1080 image (39x69 = 2,691 tokens),
+    prefix U[0,512], suffix U[16,128] (seeded), ratio 0.05; each request on its own pages."""
+    from vlcache_b200.engine import kv_cache as kvc
+    rng = np.random.default_rng(3)
+    n_img = 39 * 69
+    R3 = kvc.recompute_count(0.05, n_img)
+    reqs, page = [], 0
+    for _ in range(64):
+        pre, suf = int(rng.integers(0, 513)), int(rng.integers(16, 129))
+        n = pre + n_img + suf
+        nb = (n + BLOCK - 1) // BLOCK
+        reqs.append(kvc.WarmRequest(n, list(range(page, page + nb)), pre, pre + n_img, R3, True))
+        page += nb
+    return reqs, page, n_img, R3
+
+
+def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4):
+    """Prefill attention of the cfg3 batch (3B heads) on one GPU: µs per layer and TF/s,
+    cycling through ``distinct`` layer caches (each larger than the L2), one graph."""
+    from vlcache_b200 import ops
+    from vlcache_b200.engine import kv_cache as kvc
+    reqs, pages, _, _ = cfg3_requests()
+    batch = kvc.WarmPrefillBuilder(H, HK).build(reqs)
+    cu_q, cu_k = batch.cu_seqlens_q, batch.cu_seqlens_k
+    total_q = int(cu_q[-1])
+    g = torch.Generator(device=device).manual_seed(33)
+    caches = [(torch.randn(pages, BLOCK, HK, D, generator=g, device=device).to(torch.bfloat16),
+               torch.randn(pages, BLOCK, HK, D, generator=g, device=device).to(torch.bfloat16))
+              for _ in range(distinct)]
+    qs = [torch.randn(total_q, H, D, generator=g, device=device).to(torch.bfloat16) for _ in range(distinct)]
+    bt = torch.from_numpy(batch.block_tables).to(device)
+    plan = ops.build_prefill_plan(cu_q, cu_k, H, HK, device=device)
+    ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device=device)
+    out = torch.empty(total_q, H, D, dtype=torch.bfloat16, device=device)
+    scale = 1.0 / math.sqrt(D)
+
+    def layers():
+        for i in range(distinct):
+            ops.prefill_attention(qs[i], caches[i][0], caches[i][1], bt, plan, scale, out, ws)
+    gr = graph_of(layers)
+    ms = timed(gr.replay, reps, 3, False) / distinct
+    flop = 4 * D * H * causal_pairs(cu_q, cu_k)
+    del caches
+    return {"workload": f"cfg3: 64 warm requests (3B heads), {total_q} query rows, one layer per launch",
+            "us_per_layer": ms * 1e3, "tflops": flop / (ms * 1e-3) / 1e12, "flop_per_layer": int(flop),
+            "units": plan.num_units, "split_tiles": plan.num_merges}
 
 
 # ---------------------------------------------------------------------------- decode
@@ -597,6 +637,7 @@ def main():
     torch.cuda.empty_cache()
     dec_us, dec_gbs, dec_bytes = decode_bench(device, args.steps, warmup, dist_on)
     meta = metadata_bench(device) if rank == 0 else None
+    cfg3 = cfg3_attention_bench(device) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -630,6 +671,7 @@ def main():
                        "bytes_per_layer": dec_bytes, "peak_gbs": hbm_peak},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "metadata": meta,
+            "cfg3_attn": cfg3,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
             "device_error": err,
