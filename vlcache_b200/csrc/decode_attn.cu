@@ -483,13 +483,8 @@ extern "C" int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs
   prm.part_o = ws;
   prm.part_ml = ws ? ws + (int64_t)num_seqs * max_splits * num_heads * HD : nullptr;
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-        cudaSuccess)
-      return VLC_ERR_CUDA;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (ensure_dynamic_smem((const void*)decode_attn_kernel, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(max_splits, num_kv_heads, num_seqs);
   decode_attn_kernel<<<grid, NUM_THREADS, SMEM_BYTES, st>>>(prm);

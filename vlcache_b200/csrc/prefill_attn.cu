@@ -909,13 +909,8 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   }
   prm.tokens_per_tile = T;
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-        cudaSuccess)
-      return VLC_ERR_CUDA;
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};
+  if (ensure_dynamic_smem((const void*)prefill_attn_kernel, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   // Both kernels are launched as programmatic dependents of their predecessor in the
   // stream (the attention: of the KV scatter; the merge: of the attention).  They wait
