@@ -418,7 +418,9 @@ def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4):
 
 
 # ---------------------------------------------------------------------------- decode
-def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_graph=True):
+def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_graph=True, impl="vlcache"):
+    """cfg5 paged decode per layer; ``impl="flash_attn"`` times the reference's kernel on the
+    same data instead."""
     from vlcache_b200 import ops
     rng = np.random.default_rng(5)
     lens = rng.integers(2700, 10701, size=DEC_SEQS)
@@ -452,7 +454,18 @@ def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_grap
         for l in range(DEC_LAYERS):
             kc, vc = caches[l % distinct]
             ops.decode_attention(q[l], kc, vc, btd, ctx, max_len, scale, out[l], ws)
-    if use_graph:
+
+    if impl == "flash_attn":
+        import flash_attn as fa
+
+        def step():  # noqa: F811  (the reference's call, attention.py:71-74)
+            for l in range(DEC_LAYERS):
+                kc, vc = caches[l % distinct]
+                fa.flash_attn_with_kvcache(q[l].unsqueeze(1), kc, vc, cache_seqlens=ctx, block_table=btd,
+                                           softmax_scale=scale, causal=True)
+    if impl == "flash_attn":
+        ms, _ = _time_maybe_graph(step, steps)
+    elif use_graph:
         g_ = graph_of(step)
         ms = timed(g_.replay, steps, warmup, dist_on)
     else:
@@ -461,6 +474,50 @@ def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_grap
     us = ms * 1e3 / DEC_LAYERS
     del caches
     return us, bytes_per_layer / (us * 1e-6) / 1e9, bytes_per_layer
+
+
+# ---------------------------------------------------------------------------- reference kernels
+def _time_maybe_graph(fn, reps):
+    """Device time of ``fn`` per call: captured in a CUDA graph when it is capture-safe,
+    else eager (flagged)."""
+    try:
+        g = graph_of(fn)
+        return timed(g.replay, reps, 3, False), "graph"
+    except Exception:
+        torch.cuda.synchronize()
+        return timed(fn, reps, 3, False), "eager"
+
+
+def reference_kernels_bench(wl, device, reps: int = 10):
+    """The reference's own attention kernels (flash-attn 2.8.3: ``flash_attn_varlen_func`` with
+    ``block_table`` for prefill, ``flash_attn_with_kvcache`` for decode, called as
+    nanovllm/layers/attention.py:64-74 calls them) on this B200 with the same inputs: cfg2
+    prefill attention per layer and cfg5 decode per layer.  A comparator only."""
+    try:
+        import flash_attn as fa
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flash_attn import failed: {type(e).__name__}"}
+    res = {"impl": f"flash-attn {fa.__version__} (the reference's kernels) on this GPU"}
+    try:
+        cu_q = torch.from_numpy(wl.cu_q).to(device)
+        cu_k = torch.from_numpy(wl.cu_k).to(device)
+        max_q = int(np.diff(wl.cu_q).max())
+        max_k = int(np.diff(wl.cu_k).max())
+
+        def prefill_layers():
+            for l in range(LAYERS):
+                fa.flash_attn_varlen_func(wl.q(l), wl.kv_cache[0, l], wl.kv_cache[1, l], cu_q, cu_k, max_q, max_k,
+                                          softmax_scale=wl.scale, causal=True, block_table=wl.block_tables)
+        ms, how = _time_maybe_graph(prefill_layers, reps)
+        us = ms * 1e3 / LAYERS
+        res.update(prefill_us_per_layer=us, prefill_tflops=wl.flop_per_layer / (us * 1e-6) / 1e12,
+                   prefill_timing=how)
+        dec_us, dec_gbs, _ = decode_bench(device, reps, 3, False, distinct=1, impl="flash_attn")
+        res.update(decode_us_per_layer=dec_us, decode_gbs=dec_gbs)
+    except Exception as e:  # noqa: BLE001
+        torch.cuda.synchronize()
+        res["failed"] = f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"
+    return res
 
 
 # ---------------------------------------------------------------------------- CPU baseline
@@ -588,6 +645,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-kernels", action="store_true",
+                    help="skip timing flash-attn (the reference's kernels) on the same inputs")
     ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
@@ -633,6 +692,7 @@ def main():
     launches = wl.launches_per_step
     e2e_ms, h2d, d2h = e2e_bench(wl, max(2, args.steps // 2), warmup, dist_on)
     e2e_value = world * flop_step / (e2e_ms * 1e-3) / 1e12
+    ref_kernels = reference_kernels_bench(wl, device) if rank == 0 and not args.no_reference_kernels else None
     del step_graph, attn_graph, wl
     torch.cuda.empty_cache()
     dec_us, dec_gbs, dec_bytes = decode_bench(device, args.steps, warmup, dist_on)
@@ -672,6 +732,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "metadata": meta,
             "cfg3_attn": cfg3,
+            "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
             "device_error": err,
