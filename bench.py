@@ -562,7 +562,11 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "decode":
+    if args.only == "cfg3":
+        # BASELINE config 3 batch (64 warm requests), one layer cache, graphed launches
+        c3 = cfg3_attention_bench(device, reps=max(1, args.steps), distinct=1)
+        res.update(us_per_layer=c3["us_per_layer"], tflops=c3["tflops"])
+    elif args.only == "decode":
         us, gbs, nbytes = decode_bench(device, args.steps, max(3, args.warmup), False, distinct=1, use_graph=False)
         res.update(us_per_layer=us, hbm_gbs=gbs, bytes_per_layer=nbytes)
     elif args.only == "prefill_7b_full":
@@ -647,7 +651,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
-    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter"],
+    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
