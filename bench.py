@@ -385,9 +385,10 @@ def cfg3_requests():
     return reqs, page, n_img, R3
 
 
-def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4):
+def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4, impl: str = "vlcache"):
     """Prefill attention of the cfg3 batch (3B heads) on one GPU: µs per layer and TF/s,
-    cycling through ``distinct`` layer caches (each larger than the L2), one graph."""
+    cycling through ``distinct`` layer caches (each larger than the L2), one graph;
+    ``impl="flash_attn"`` times the reference's kernel on the same data instead."""
     from vlcache_b200 import ops
     from vlcache_b200.engine import kv_cache as kvc
     reqs, pages, _, _ = cfg3_requests()
@@ -408,8 +409,21 @@ def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4):
     def layers():
         for i in range(distinct):
             ops.prefill_attention(qs[i], caches[i][0], caches[i][1], bt, plan, scale, out, ws)
-    gr = graph_of(layers)
-    ms = timed(gr.replay, reps, 3, False) / distinct
+
+    if impl == "flash_attn":
+        import flash_attn as fa
+        cu_qd = torch.from_numpy(cu_q).to(device)
+        cu_kd = torch.from_numpy(cu_k).to(device)
+        max_q, max_k = int(np.diff(cu_q).max()), int(np.diff(cu_k).max())
+
+        def layers():  # noqa: F811  (the reference's call, attention.py:64-70)
+            for i in range(distinct):
+                fa.flash_attn_varlen_func(qs[i], caches[i][0], caches[i][1], cu_qd, cu_kd, max_q, max_k,
+                                          softmax_scale=scale, causal=True, block_table=bt)
+        ms = _time_maybe_graph(layers, reps)[0] / distinct
+    else:
+        gr = graph_of(layers)
+        ms = timed(gr.replay, reps, 3, False) / distinct
     flop = 4 * D * H * causal_pairs(cu_q, cu_k)
     del caches
     return {"workload": f"cfg3: 64 warm requests (3B heads), {total_q} query rows, one layer per launch",
@@ -514,6 +528,8 @@ def reference_kernels_bench(wl, device, reps: int = 10):
                    prefill_timing=how)
         dec_us, dec_gbs, _ = decode_bench(device, reps, 3, False, distinct=1, impl="flash_attn")
         res.update(decode_us_per_layer=dec_us, decode_gbs=dec_gbs)
+        c3 = cfg3_attention_bench(device, reps=reps, distinct=4, impl="flash_attn")
+        res.update(cfg3_us_per_layer=c3["us_per_layer"], cfg3_tflops=c3["tflops"])
     except Exception as e:  # noqa: BLE001
         torch.cuda.synchronize()
         res["failed"] = f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"
