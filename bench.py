@@ -502,6 +502,41 @@ def _time_maybe_graph(fn, reps):
         return timed(fn, reps, 3, False), "eager"
 
 
+def rope_scatter_bench(device, reps: int = 20, layers: int = 4):
+    """vlc_rope_store_kvcache (RoPE of the recomputed rows fused with the KV scatter) on the
+    cfg2 (3B, 1,123 rows) and cfg4 ratio-1.0 (7B, 10,617 rows) shapes: us per layer and the
+    HBM rate of its algorithmic bytes (every q/k/v element read and written once, plus the
+    int64 position and int32 slot of each row).  ``layers`` distinct layers' inputs rotate,
+    so the 7B inputs (4 x 98 MB) exceed the L2."""
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+    max_pos = 32768
+    table = rope_cos_sin_cache(D, max_pos, 1e6).to(device)
+    res = {}
+    for name, n, h, hk in (("cfg2", int(warm_meta()[0][-1]), H, HK), ("7b_full", SEQLEN, 28, 4)):
+        g = torch.Generator(device=device).manual_seed(5)
+        qkv = [torch.randn(n, (h + 2 * hk) * D, generator=g, device=device).to(torch.bfloat16) for _ in range(layers)]
+        pos = torch.randint(0, max_pos, (n,), generator=g, device=device)
+        nb = (n + BLOCK - 1) // BLOCK
+        kc = torch.empty(layers, nb, BLOCK, hk, D, dtype=torch.bfloat16, device=device)
+        vc = torch.empty_like(kc)
+        slots = torch.randperm(nb * BLOCK, generator=g, device=device)[:n].to(torch.int32)
+        qo = torch.empty(n, h, D, dtype=torch.bfloat16, device=device)
+
+        def fn():
+            for l in range(layers):
+                x = qkv[l]
+                ops.rope_store_kvcache(pos, x[:, :h * D].view(n, h, D), x[:, h * D:(h + hk) * D].view(n, hk, D),
+                                       x[:, (h + hk) * D:].view(n, hk, D), table, kc[l], vc[l], slots, out=qo)
+        ms, how = _time_maybe_graph(fn, reps)
+        us = ms * 1e3 / layers
+        nbytes = 2 * n * (h + 2 * hk) * D * 2 + n * 12
+        res[name] = {"rows": n, "heads": [h, hk], "us_per_layer": us, "hbm_gbs": nbytes / (us * 1e-6) / 1e9,
+                     "bytes_per_layer": nbytes, "timing": how}
+        del qkv, kc, vc
+    return res
+
+
 def reference_kernels_bench(wl, device, reps: int = 10):
     """The reference's own attention kernels (flash-attn 2.8.3: ``flash_attn_varlen_func`` with
     ``block_table`` for prefill, ``flash_attn_with_kvcache`` for decode, called as
@@ -578,7 +613,10 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "cfg3":
+    if args.only == "rope":
+        # RoPE + KV scatter of the recomputed rows (cfg2 and 7B cfg4 ratio-1.0 shapes)
+        res.update(rope_scatter_bench(device, reps=max(1, args.steps)))
+    elif args.only == "cfg3":
         # BASELINE config 3 batch (64 warm requests), one layer cache, graphed launches
         c3 = cfg3_attention_bench(device, reps=max(1, args.steps), distinct=1)
         res.update(us_per_layer=c3["us_per_layer"], tflops=c3["tflops"])
@@ -667,7 +705,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
-    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3"],
+    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -718,6 +756,10 @@ def main():
     dec_us, dec_gbs, dec_bytes = decode_bench(device, args.steps, warmup, dist_on)
     meta = metadata_bench(device) if rank == 0 else None
     cfg3 = cfg3_attention_bench(device) if rank == 0 else None
+    rope = rope_scatter_bench(device) if rank == 0 else None
+    if rope is not None:
+        for r in rope.values():
+            r["frac"] = r["hbm_gbs"] / hbm_peak
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -752,6 +794,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "metadata": meta,
             "cfg3_attn": cfg3,
+            "rope_scatter": rope,
             "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,
             "clocks": clocks,

@@ -43,6 +43,7 @@ extern "C" {
 /* ---- device error codes (recorded by kernels, read by vlc_get_device_error) ---- */
 #define VLC_DEV_ERR_SLOT_RANGE 101   /* slot >= num_slots or < -1 */
 #define VLC_DEV_ERR_BLOCK_RANGE 102  /* block table entry out of range where a key is needed */
+#define VLC_DEV_ERR_POSITION 103     /* rotary position outside the cos/sin cache */
 #define VLC_DEV_ERR_TIMEOUT 110      /* an mbarrier wait hit its bound (base; +role id) */
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -76,6 +77,26 @@ int vlc_selftest_bounded_wait(long long limit_cycles, int arrive, void* stream);
 int vlc_store_kvcache(const void* key, int64_t key_stride, const void* value, int64_t value_stride,
                       void* k_cache, void* v_cache, const int32_t* slot_mapping, int num_tokens,
                       int row_elems, int64_t num_slots, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Rotary embedding fused with the KV scatter.
+ * Replaces RotaryEmbedding.forward (nanovllm/layers/rotary_embedding.py:37-48,
+ * rotate-half apply_rotary_emb :6-14) followed by store_kvcache (attention.py:10-40):
+ *   q_out[i] = rope(q[i], positions[i])        (q_out may be q: in place)
+ *   slot_mapping != NULL: rope(key[i]) and value[i] to k_cache / v_cache row
+ *                         slot_mapping[i] (-1 skipped; rows of num_kv_heads*head_dim)
+ *   slot_mapping == NULL: rope(key[i]) to k_out[i] (value, caches unused)
+ * positions: int64 [num_tokens]; cos_sin_cache: fp32 [max_position, head_dim]
+ * (first half cos, second half sin, as the reference's buffer); head_dim ==
+ * rotary_dim == 128.  Strides are token strides in elements.  fp32 math with each
+ * product and sum rounded separately, bf16 round-to-nearest-even output.
+ * ------------------------------------------------------------------------ */
+int vlc_rope_store_kvcache(const int64_t* positions, const void* q, int64_t q_stride, void* q_out,
+                           int64_t q_out_stride, const void* key, int64_t key_stride, const void* value,
+                           int64_t value_stride, const float* cos_sin_cache, int64_t max_position,
+                           int rotary_dim, void* k_cache, void* v_cache, const int32_t* slot_mapping,
+                           int64_t num_slots, void* k_out, int64_t k_out_stride, int num_tokens,
+                           int num_heads, int num_kv_heads, int head_dim, void* stream);
 
 /* --------------------------------------------------------------------------
  * M-RoPE position shift of reused vision K (new capability; replaces the

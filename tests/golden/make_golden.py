@@ -15,6 +15,10 @@ What is captured (all small):
     (Qwen2_5_VLRotaryEmbedding + apply_multimodal_rotary_pos_emb +
     get_vision_position_ids) applied to seeded keys of a 32x32 merged grid at vision
     start 0 and at start 16.
+  * rope_3b.npz — nano-vllm's own 1-D RoPE (nanovllm/layers/rotary_embedding.py):
+    rows of the ``RotaryEmbedding`` cos_sin_cache buffer (:29-35, theta 1e6, head 128)
+    at seeded positions, and ``apply_rotary_emb`` (:6-14) of seeded bf16 query/key rows
+    with cos | sin gathered as ``forward`` does (:37-48), evaluated eagerly on the CPU.
   * attention_cfg1.npz — checksums of the fp32 oracle attention of config 1
     (the reference's flash-attn path needs a GPU; the attention oracle is a
     restatement, so this file is a regression pin for it).
@@ -200,6 +204,26 @@ def run_mrope_cfg1():
                         inv_freq=rot.inv_freq.numpy().astype(np.float32))
 
 
+def run_rope():
+    from nanovllm.layers.rotary_embedding import RotaryEmbedding, apply_rotary_emb
+
+    max_pos = 32768
+    rot = RotaryEmbedding(128, 128, max_pos, 1e6)   # only the table: forward is torch.compile'd
+    g = torch.Generator().manual_seed(7)
+    n, h, hk = 24, 4, 2
+    pos = torch.randint(0, max_pos, (n,), generator=g, dtype=torch.int64)
+    pos[:4] = torch.tensor([0, 1, max_pos - 1, 10617])
+    q = torch.randn(n, h, 128, generator=g).mul_(3).to(torch.bfloat16)
+    k = torch.randn(n, hk, 128, generator=g).mul_(3).to(torch.bfloat16)
+    cos, sin = rot.cos_sin_cache[pos].chunk(2, dim=-1)       # as forward (:44-45)
+    q_ref = apply_rotary_emb(q, cos, sin)
+    k_ref = apply_rotary_emb(k, cos, sin)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    np.savez_compressed(HERE / "rope_3b.npz", max_position=np.int64(max_pos), positions=pos.numpy(),
+                        cos_sin_rows=rot.cos_sin_cache[pos, 0].numpy().astype(np.float32),
+                        q=bits(q), k=bits(k), q_rot=bits(q_ref), k_rot=bits(k_ref))
+
+
 def run_attention_cfg1():
     sys.path.insert(0, str(REPO))
     from oracle import attention as oatt
@@ -215,8 +239,14 @@ def run_attention_cfg1():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the VLCache reference checkout")
+    ap.add_argument("--only", default=None, choices=["decode", "mrope", "rope", "attention"],
+                    help="regenerate one fixture family only")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
+    if args.only:
+        {"decode": run_decode_scenario, "mrope": run_mrope_cfg1, "rope": run_rope,
+         "attention": run_attention_cfg1}[args.only]()
+        return
     # BASELINE config 2 shape: 20 + 10,549 (77x137) + 48, ratio 0.1; cold copy at prefix 12
     run_metadata_scenario("cfg2", cold_prefix=12, warm_specs=[(20, 77 * 137, 48, True)], ratio=0.1)
     # config 1 shape under the reference rule R = ceil(0.1 * 1024) = 103
@@ -226,6 +256,7 @@ def main():
                                                               (511, 2691, 128, True)], ratio=0.05, seed=2)
     run_decode_scenario()
     run_mrope_cfg1()
+    run_rope()
     run_attention_cfg1()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)

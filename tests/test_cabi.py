@@ -47,6 +47,13 @@ def test_argument_errors_are_reported_before_launch(cuda_lib):
     assert cuda_lib.vlc_mrope_shift(one, None, 0, 1, 16, 2, 128, one, None, 1, d, sec, 1e6, None) == 2
     assert cuda_lib.vlc_decode_attn(one, 128, 1, 16, one, one, 256, 2, 64, one, 1, 256, one, 10, 1.0, one,
                                     128, None, 0, None) == 5
+    # rotary + scatter: head_dim 64 unsupported (5), NULL query (1), fused mode without caches (1)
+    assert cuda_lib.vlc_rope_store_kvcache(one, one, 512, one, 512, one, 128, one, 128, one, 64, 64, one, one, one,
+                                           16, None, 0, 4, 4, 1, 64, None) == 5
+    assert cuda_lib.vlc_rope_store_kvcache(one, None, 512, one, 512, one, 128, one, 128, one, 64, 128, one, one,
+                                           one, 16, None, 0, 4, 4, 1, 128, None) == 1
+    assert cuda_lib.vlc_rope_store_kvcache(one, one, 512, one, 512, one, 128, one, 128, one, 64, 128, None, None,
+                                           one, 16, None, 0, 4, 4, 1, 128, None) == 1
     plan = np.zeros(32, np.int32)
     assert cuda_lib.vlc_prefill_attn(one, 2048, 1, 16, one, one, 256, 256, 256, 2, 128, one, 1, 256, one,
                                      plan.ctypes.data, 1.0, one, 2048, None, 0, None) == 8

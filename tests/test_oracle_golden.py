@@ -9,6 +9,7 @@ import torch
 from oracle import attention as oatt
 from oracle import metadata as omd
 from oracle import mrope as omr
+from oracle import rope as orope
 
 GOLD = Path(__file__).resolve().parent / "golden"
 
@@ -139,3 +140,33 @@ def test_attention_oracle_semantics_small():
         ref = torch.softmax(s, -1) @ v[0, :p + 1, 0]
         assert torch.allclose(out[i], ref, atol=1e-5)
     assert oatt.causal_pairs([0, 1075, 1123], [0, 1075, 11692]) == 1086838
+
+
+def test_rope_oracle_and_table_match_reference():
+    """nano-vllm's RoPE (rotary_embedding.py:6-14, 29-48), evaluated eagerly by the
+    reference itself: the cos/sin table this package builds and the oracle's rotation
+    match it bit for bit."""
+    from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+    f = np.load(GOLD / "rope_3b.npz")
+    table = rope_cos_sin_cache(128, int(f["max_position"]), 1e6)
+    pos = f["positions"]
+    assert table.shape == (int(f["max_position"]), 1, 128) and table.dtype == torch.float32
+    assert np.array_equal(table[pos, 0].numpy().view(np.uint32), f["cos_sin_rows"].view(np.uint32))
+    assert np.array_equal(orope.rope_rows(f["q"], pos, table[:, 0].numpy()), f["q_rot"])
+    assert np.array_equal(orope.rope_rows(f["k"], pos, table[:, 0].numpy()), f["k_rot"])
+
+
+def test_rope_store_oracle_skips_minus_one_slots():
+    g = np.random.default_rng(3)
+    n, hk, d = 5, 2, 128
+    table = np.zeros((16, d), np.float32)
+    table[:, : d // 2] = 1.0                       # cos 1, sin 0: rotation is the identity
+    q = g.integers(0, 0x4000, (n, 4, d), dtype=np.uint16)
+    k = g.integers(0, 0x4000, (n, hk, d), dtype=np.uint16)
+    v = g.integers(0, 0x4000, (n, hk, d), dtype=np.uint16)
+    kc = np.zeros((8, hk * d), np.uint16)
+    q_out, kc2, vc2 = orope.rope_store_kvcache(np.arange(n), q, k, v, table, kc, kc, np.array([3, -1, 0, 7, -1]))
+    assert np.array_equal(q_out, q)
+    assert np.array_equal(kc2[[3, 0, 7]], k[[0, 2, 3]].reshape(3, -1))
+    assert np.array_equal(vc2[[3, 0, 7]], v[[0, 2, 3]].reshape(3, -1))
+    assert not kc2[[1, 2, 4, 5, 6]].any()

@@ -26,6 +26,9 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_selftest_bounded_wait": (c_int, [c_i64, c_int, c_vp]),
     "vlc_num_sms": (c_int, []),
     "vlc_store_kvcache": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_i64, c_vp]),
+    "vlc_rope_store_kvcache": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                       c_int, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_int,
+                                       c_vp]),
     "vlc_mrope_shift": (c_int, [c_vp, c_vp, c_i64, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_int,
                                 c_vp, c_vp, c_float, c_vp]),
     "vlc_prefill_plan": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_vp, c_i64, c_vp]),

@@ -155,6 +155,113 @@ __global__ void __launch_bounds__(256) mrope_shift_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Rotary embedding of new rows fused with the paged KV scatter.
+// Semantics of nanovllm/layers/rotary_embedding.py:6-14 + 37-48 (apply_rotary_emb on
+// query and key, cos/sin gathered from cos_sin_cache[positions]) followed by
+// store_kvcache (nanovllm/layers/attention.py:10-40):
+//   q_out[i] = rope(q[i], positions[i]);  the K row roped and the V row copied to
+//   k_cache / v_cache row slot_mapping[i] (slot -1: neither stored).
+// Without slot_mapping the roped K rows go to k_out instead (RotaryEmbedding.forward).
+// cos_sin_cache rows are the caller's [max_position, 128] fp32 (64 cos | 64 sin).  Each
+// fp32 product, sum and difference is rounded on its own (no FMA contraction), as the
+// reference function evaluates them op by op, and the result is rounded to bf16 to
+// nearest even.  Thread = 8 rotate-half pairs (j, j + 64) of one head in kRopeTokens
+// consecutive tokens: two 16-byte loads and stores per token, all loads issued before
+// any math; a token group's threads cover its query heads, then its key heads, then
+// its value heads (copied).
+// ---------------------------------------------------------------------------
+constexpr int kRopeDim = 128;                 // head_dim == rotary_dim
+constexpr int kRopeThreads = kRopeDim / 16;   // threads per head (8 pairs each)
+constexpr int kRopeTokens = 2;                // tokens per thread: all their loads issued first
+
+__global__ void __launch_bounds__(256) rope_store_kvcache_kernel(
+    const int64_t* __restrict__ positions, const __nv_bfloat16* q, int64_t q_stride, __nv_bfloat16* q_out,
+    int64_t q_out_stride, const __nv_bfloat16* key, int64_t key_stride, const __nv_bfloat16* __restrict__ value,
+    int64_t value_stride, const float* __restrict__ cos_sin, int64_t max_position,
+    __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+    const int32_t* __restrict__ slot_mapping, int64_t num_slots, __nv_bfloat16* k_out, int64_t k_out_stride,
+    int num_tokens, int num_heads, int num_kv_heads) {
+  pdl_launch_dependents();  // the attention that follows may start its prologue
+  const int per_group = (num_heads + 2 * num_kv_heads) * kRopeThreads;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t groups = ((int64_t)num_tokens + kRopeTokens - 1) / kRopeTokens;
+  if (gid >= groups * per_group) return;
+  const int64_t grp = gid / per_group;
+  const int u = (int)(gid - grp * per_group);
+  const int head = u / kRopeThreads;  // query heads, key heads, value heads
+  const int c = u - head * kRopeThreads;
+  const bool is_q = head < num_heads;
+  const bool is_v = head >= num_heads + num_kv_heads;
+  const int kh = head - num_heads;                 // key head (is_q false, is_v false)
+  const int vh = head - num_heads - num_kv_heads;  // value head (is_v)
+  const int64_t row_elems = (int64_t)num_kv_heads * kRopeDim;
+  constexpr int half = kRopeDim / 2;
+  __nv_bfloat16* const dst_base = is_v ? v_cache : is_q ? q_out : slot_mapping != nullptr ? k_cache : k_out;
+  uint4 a[kRopeTokens], b[kRopeTokens];
+  int64_t dst_off[kRopeTokens], pos[kRopeTokens];
+#pragma unroll
+  for (int t = 0; t < kRopeTokens; ++t) {
+    const int token = (int)(grp * kRopeTokens + t);
+    dst_off[t] = -1;  // nothing to store
+    pos[t] = 0;
+    if (token >= num_tokens) continue;
+    int64_t slot = -1;
+    if (slot_mapping != nullptr) {
+      slot = __ldg(slot_mapping + token);
+      if (slot < -1 || slot >= num_slots) {
+        if (u == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
+        slot = -1;
+      }
+    }
+    const __nv_bfloat16* src;
+    if (is_v) {  // copied with its K row
+      if (slot < 0) continue;
+      src = value + (int64_t)token * value_stride + vh * kRopeDim;
+      dst_off[t] = slot * row_elems + vh * kRopeDim;
+    } else {
+      if (!is_q && slot_mapping != nullptr && slot < 0) continue;  // K row not stored
+      pos[t] = __ldg(positions + token);
+      if (pos[t] < 0 || pos[t] >= max_position) {
+        if (u == 0) record_error(VLC_DEV_ERR_POSITION);
+        continue;
+      }
+      src = is_q ? q + (int64_t)token * q_stride + head * kRopeDim : key + (int64_t)token * key_stride + kh * kRopeDim;
+      dst_off[t] = is_q ? (int64_t)token * q_out_stride + head * kRopeDim
+                   : slot_mapping != nullptr ? slot * row_elems + kh * kRopeDim
+                                             : (int64_t)token * k_out_stride + kh * kRopeDim;
+    }
+    a[t] = *reinterpret_cast<const uint4*>(src + 8 * c);
+    b[t] = *reinterpret_cast<const uint4*>(src + half + 8 * c);
+  }
+#pragma unroll
+  for (int t = 0; t < kRopeTokens; ++t) {
+    if (dst_off[t] < 0) continue;
+    __nv_bfloat16* dst = dst_base + dst_off[t];
+    if (!is_v) {
+      const float4* cs = reinterpret_cast<const float4*>(cos_sin + pos[t] * kRopeDim);
+      const float4 c0 = __ldg(cs + 2 * c), c1 = __ldg(cs + 2 * c + 1);
+      const float4 s0 = __ldg(cs + half / 4 + 2 * c), s1 = __ldg(cs + half / 4 + 2 * c + 1);
+      const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float x1[8], x2[8];
+      unpack8(a[t], x1);
+      unpack8(b[t], x2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float y1 = __fsub_rn(__fmul_rn(x1[i], cv[i]), __fmul_rn(x2[i], sv[i]));
+        const float y2 = __fadd_rn(__fmul_rn(x2[i], cv[i]), __fmul_rn(x1[i], sv[i]));
+        x1[i] = y1;
+        x2[i] = y2;
+      }
+      a[t] = pack8(x1);
+      b[t] = pack8(x2);
+    }
+    *reinterpret_cast<uint4*>(dst + 8 * c) = a[t];
+    *reinterpret_cast<uint4*>(dst + half + 8 * c) = b[t];
+  }
+}
+
 // inv_freq[j] in fp32 exactly as the RoPE reference builds it:
 //   1 / (theta ** (float(2j) / float(dim)))
 static float inv_freq_f32(float theta, int j, int head_dim) {
@@ -183,6 +290,43 @@ extern "C" int vlc_store_kvcache(const void* key, int64_t key_stride, const void
   store_kvcache_kernel<<<grid, warps * 32, 0, (cudaStream_t)stream>>>(
       (const uint4*)key, key_stride / 8, (const uint4*)value, value_stride / 8, (uint4*)k_cache,
       (uint4*)v_cache, slot_mapping, num_tokens, row_elems / 8, num_slots);
+  return launch_status();
+}
+
+extern "C" int vlc_rope_store_kvcache(const int64_t* positions, const void* q, int64_t q_stride, void* q_out,
+                                      int64_t q_out_stride, const void* key, int64_t key_stride,
+                                      const void* value, int64_t value_stride, const float* cos_sin_cache,
+                                      int64_t max_position, int rotary_dim, void* k_cache, void* v_cache,
+                                      const int32_t* slot_mapping, int64_t num_slots, void* k_out,
+                                      int64_t k_out_stride, int num_tokens, int num_heads, int num_kv_heads,
+                                      int head_dim, void* stream) {
+  if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || max_position <= 0) return VLC_ERR_SHAPE;
+  if (head_dim != kRopeDim || rotary_dim != head_dim) return VLC_ERR_UNSUPPORTED;
+  if (num_tokens == 0) return VLC_OK;
+  if (!positions || !q || !q_out || !key || !cos_sin_cache) return VLC_ERR_NULL;
+  const bool fused = slot_mapping != nullptr;
+  if (fused ? (!value || !k_cache || !v_cache) : !k_out) return VLC_ERR_NULL;
+  if (fused && num_slots <= 0) return VLC_ERR_SHAPE;
+  if (q_stride % 8 || q_out_stride % 8 || key_stride % 8 || (fused && value_stride % 8) ||
+      (!fused && k_out_stride % 8))
+    return VLC_ERR_STRIDE;
+  if (q_stride < (int64_t)num_heads * head_dim || q_out_stride < (int64_t)num_heads * head_dim ||
+      key_stride < (int64_t)num_kv_heads * head_dim || (fused && value_stride < (int64_t)num_kv_heads * head_dim) ||
+      (!fused && k_out_stride < (int64_t)num_kv_heads * head_dim))
+    return VLC_ERR_STRIDE;
+  if (!aligned16(q) || !aligned16(q_out) || !aligned16(key) || !aligned16(cos_sin_cache) ||
+      (fused && (!aligned16(value) || !aligned16(k_cache) || !aligned16(v_cache))) || (!fused && !aligned16(k_out)))
+    return VLC_ERR_ALIGN;
+  const int64_t threads =
+      ((int64_t)num_tokens + kRopeTokens - 1) / kRopeTokens * (num_heads + 2 * num_kv_heads) * kRopeThreads;
+  const int block = 256;
+  const int64_t grid = (threads + block - 1) / block;
+  if (grid > 0x7fffffff) return VLC_ERR_SHAPE;
+  rope_store_kvcache_kernel<<<(unsigned)grid, block, 0, (cudaStream_t)stream>>>(
+      positions, (const __nv_bfloat16*)q, q_stride, (__nv_bfloat16*)q_out, q_out_stride,
+      (const __nv_bfloat16*)key, key_stride, (const __nv_bfloat16*)value, value_stride, cos_sin_cache,
+      max_position, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, slot_mapping, num_slots,
+      (__nv_bfloat16*)k_out, k_out_stride, num_tokens, num_heads, num_kv_heads);
   return launch_status();
 }
 

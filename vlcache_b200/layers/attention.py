@@ -7,6 +7,10 @@ device steps run in this library's sm_100a kernels instead of Triton/flash-attn:
   * ``store_kvcache``  (reference :10-40, Triton)      -> vlc_store_kvcache
   * prefill            (reference :64-70, flash-attn)  -> vlc_prefill_attn (tcgen05)
   * decode             (reference :71-74, flash-attn)  -> vlc_decode_attn (split-K)
+Optionally ``forward(q, k, v, positions=..., rotary_emb=...)`` takes q/k before RoPE
+and rotates them in the scatter launch (vlc_rope_store_kvcache): the caller's
+``q, k = self.rotary_emb(positions, q, k); o = self.attn(q, k, v)``
+(nanovllm/models/qwen3.py:84-86) becomes one call with the same result.
 """
 from __future__ import annotations
 
@@ -63,7 +67,8 @@ class Attention(nn.Module):
         self.k_cache = self.v_cache = torch.tensor([])
         self.layer_id = None  # set by engine.kv_cache.allocate_kv_cache (or the caller)
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor | None = None,
+                rotary_emb: nn.Module | None = None):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
         if context.kv_ready is not None:    # this layer's reused rows are placed
@@ -71,7 +76,17 @@ class Attention(nn.Module):
             # successor in the stream, so its programmatic launch overlaps the scatter)
             assert self.layer_id is not None, "kv_ready needs Attention.layer_id"
             torch.cuda.current_stream().wait_event(context.kv_ready[self.layer_id])
-        if k_cache.numel() and v_cache.numel():
+        have_cache = bool(k_cache.numel() and v_cache.numel())
+        if rotary_emb is not None:
+            assert positions is not None, "rotary_emb needs the positions"
+            if have_cache and (context.block_tables is not None or not context.is_prefill):
+                # K/V are read back from the cache: rotate and scatter in one launch
+                q = ops.rope_store_kvcache(positions, q, k, v, rotary_emb.cos_sin_cache, k_cache, v_cache,
+                                           context.slot_mapping)
+                have_cache = False  # stored
+            else:                   # cold prefill reads the in-flight K: rotate it too
+                q, k = rotary_emb(positions, q, k)
+        if have_cache:
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if context.is_prefill:
             plan = _prefill_plan(context, self.num_heads, self.num_kv_heads, q.device)

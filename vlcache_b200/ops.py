@@ -63,6 +63,71 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
     check("vlc_store_kvcache", st)
 
 
+# --------------------------------------------------------------------------- rotary + scatter
+def _rope_args(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor, cos_sin_cache: torch.Tensor):
+    N, H, D = query.shape
+    Hk = key.shape[1]
+    assert key.shape[0] == N and key.shape[2] == D and positions.numel() == N
+    assert query.stride(-1) == 1 and query.stride(1) == D and key.stride(-1) == 1 and key.stride(1) == D
+    assert query.dtype == torch.bfloat16 and key.dtype == torch.bfloat16
+    assert positions.dtype == torch.int64 and positions.is_contiguous()
+    assert cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous()
+    assert cos_sin_cache.shape[-1] == D and cos_sin_cache.numel() == cos_sin_cache.shape[0] * D
+    return N, H, Hk, D, cos_sin_cache.shape[0]
+
+
+def rotary_embedding(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                     cos_sin_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rotate-half RoPE of ``query`` [N, H, D] and ``key`` [N, Hk, D] at ``positions``.
+
+    Semantics of nanovllm/layers/rotary_embedding.py:37-48 (``cos_sin_cache[positions]``
+    split into cos | sin, ``apply_rotary_emb`` :6-14 in fp32, result in bf16); returns new
+    tensors like the reference.  ``cos_sin_cache`` is the reference's buffer
+    ([max_position, 1, D] fp32) or the same values as [max_position, D].
+    """
+    _require_cuda(positions, query, key, cos_sin_cache)
+    N, H, Hk, D, max_pos = _rope_args(positions, query, key, cos_sin_cache)
+    q_out = torch.empty((N, H, D), dtype=query.dtype, device=query.device)
+    k_out = torch.empty((N, Hk, D), dtype=key.dtype, device=key.device)
+    st = lib().vlc_rope_store_kvcache(_ptr(positions), _ptr(query), query.stride(0), _ptr(q_out), q_out.stride(0),
+                                      _ptr(key), key.stride(0), None, 0, _ptr(cos_sin_cache), max_pos, D, None,
+                                      None, None, 0, _ptr(k_out), k_out.stride(0), N, H, Hk, D, _stream())
+    check("vlc_rope_store_kvcache", st)
+    return q_out, k_out
+
+
+def rope_store_kvcache(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                       cos_sin_cache: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       slot_mapping: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE of ``query`` and ``key`` fused with the paged KV scatter: returns the roped
+    query (into ``out`` when given; ``out`` may be ``query``) and writes the roped key
+    and the value rows to ``k_cache`` / ``v_cache`` row ``slot_mapping[i]`` (-1 skipped).
+
+    One launch for what the reference does in two steps: ``rotary_emb(positions, q, k)``
+    (rotary_embedding.py:37-48) and ``store_kvcache`` (attention.py:10-40, with its
+    stride assertions :33-40).  The key's K rows reach the cache roped, bit-identical to
+    roping then scattering.
+    """
+    _require_cuda(positions, query, key, value, cos_sin_cache, k_cache, v_cache, slot_mapping)
+    N, H, Hk, D, max_pos = _rope_args(positions, query, key, cos_sin_cache)
+    assert value.shape == key.shape and value.stride(-1) == 1 and value.stride(1) == D
+    assert value.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16 and v_cache.dtype == torch.bfloat16
+    row = Hk * D
+    assert k_cache.stride(1) == row and v_cache.stride(1) == row    # as store_kvcache (attention.py:33-40)
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.numel() == N and slot_mapping.is_contiguous()
+    if out is None:
+        out = torch.empty((N, H, D), dtype=query.dtype, device=query.device)
+    assert out.shape == (N, H, D) and out.stride(-1) == 1 and out.stride(1) == D
+    num_slots = k_cache.numel() // row
+    st = lib().vlc_rope_store_kvcache(_ptr(positions), _ptr(query), query.stride(0), _ptr(out), out.stride(0),
+                                      _ptr(key), key.stride(0), _ptr(value), value.stride(0), _ptr(cos_sin_cache),
+                                      max_pos, D, _ptr(k_cache), _ptr(v_cache), _ptr(slot_mapping), num_slots,
+                                      None, 0, N, H, Hk, D, _stream())
+    check("vlc_rope_store_kvcache", st)
+    return out
+
+
 # --------------------------------------------------------------------------- M-RoPE shift
 def mrope_shift(k_cache: torch.Tensor, v_cache: torch.Tensor | None, src_slots: torch.Tensor,
                 dst_slots: torch.Tensor | None, delta_thw, mrope_section=DEFAULT_MROPE_SECTION,
