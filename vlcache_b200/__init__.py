@@ -3,7 +3,9 @@
 Drop-in for the attention hot path of VLCache / nano-vllm:
   * ``vlcache_b200.layers.attention``        — ``Attention`` / ``store_kvcache``
   * ``vlcache_b200.utils.context``           — ``set_context`` / ``get_context``
-  * ``vlcache_b200.layers.rotary_embedding`` — M-RoPE position shift of reused image K
+  * ``vlcache_b200.layers.rotary_embedding`` — ``RotaryEmbedding`` / ``get_rope`` (RoPE of new
+                                               rows, optionally fused with the KV scatter) and
+                                               the M-RoPE position shift of reused image K
   * ``vlcache_b200.engine.kv_cache``         — KV-cache allocation, image-KV reuse copy,
                                                warm-prefill metadata
 All compute runs in the hand-written CUDA kernels of ``libvlcache_b200.so`` (C ABI in
