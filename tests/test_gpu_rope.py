@@ -141,3 +141,39 @@ def test_attention_forward_fused_rope_equals_unfused(cuda_lib):
     assert torch.equal(outs[0][0], outs[1][0])
     assert ops.device_error() == 0
     ctx.reset_context()
+
+
+def test_attention_forward_decode_fused_rope(cuda_lib):
+    """Decode through the fused path: the new token's rotated K lands in its slot and the
+    output equals the unfused path (rotate, then scatter and attend) bit for bit."""
+    from tests.helpers import make_decode_case
+    from vlcache_b200 import ops
+    from vlcache_b200.engine import kv_cache as kvc
+    from vlcache_b200.layers.attention import Attention
+    from vlcache_b200.layers.rotary_embedding import RotaryEmbedding
+    from vlcache_b200.utils import context as ctx
+    H, Hk, D = 28, 4, 128
+    lens = [5000, 257, 1, 3000]
+    q, kc, vc, bt, _, scale = make_decode_case(len(lens), H, Hk, lens, seed=23)
+    g = torch.Generator().manual_seed(24)
+    k_new = torch.randn(len(lens), Hk, D, generator=g).to(torch.bfloat16).cuda()
+    v_new = torch.randn(len(lens), Hk, D, generator=g).to(torch.bfloat16).cuda()
+    bts = [[int(x) for x in row if x >= 0] for row in bt.tolist()]
+    positions = kvc.prepare_decode(lens, bts, device="cuda")
+    rot = RotaryEmbedding(D, D, 8192, 1e6).cuda()
+    outs = []
+    for fused in (False, True):
+        attn = Attention(H, D, scale, Hk)
+        attn.k_cache, attn.v_cache = kc.cuda(), vc.cuda()
+        if fused:
+            o = attn(q.cuda(), k_new, v_new, positions=positions, rotary_emb=rot)
+        else:
+            qr, kr = rot(positions, q.cuda(), k_new)
+            o = attn(qr, kr, v_new)
+        torch.cuda.synchronize()
+        outs.append((o, attn.k_cache, attn.v_cache))
+    assert outs[1][0].shape == (len(lens), 1, H, D)
+    assert torch.equal(outs[0][1], outs[1][1]) and torch.equal(outs[0][2], outs[1][2])
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert ops.device_error() == 0
+    ctx.reset_context()
