@@ -198,41 +198,43 @@ __global__ void __launch_bounds__(256) rope_store_kvcache_kernel(
   const int64_t row_elems = (int64_t)num_kv_heads * kRopeDim;
   constexpr int half = kRopeDim / 2;
   __nv_bfloat16* const dst_base = is_v ? v_cache : is_q ? q_out : slot_mapping != nullptr ? k_cache : k_out;
+  // First every load that depends on nothing: the row chunks, slots and positions of all
+  // the thread's tokens go out together (one memory latency), then the checks.
   uint4 a[kRopeTokens], b[kRopeTokens];
-  int64_t dst_off[kRopeTokens], pos[kRopeTokens];
+  int64_t slot[kRopeTokens], pos[kRopeTokens], dst_off[kRopeTokens];
+#pragma unroll
+  for (int t = 0; t < kRopeTokens; ++t) {
+    const int token = (int)(grp * kRopeTokens + t);
+    slot[t] = -1;
+    pos[t] = 0;
+    if (token >= num_tokens || (is_v && slot_mapping == nullptr)) continue;  // no value rows to copy
+    const __nv_bfloat16* src = is_v ? value + (int64_t)token * value_stride + vh * kRopeDim
+                               : is_q ? q + (int64_t)token * q_stride + head * kRopeDim
+                                      : key + (int64_t)token * key_stride + kh * kRopeDim;
+    a[t] = *reinterpret_cast<const uint4*>(src + 8 * c);
+    b[t] = *reinterpret_cast<const uint4*>(src + half + 8 * c);
+    if (!is_q && slot_mapping != nullptr) slot[t] = __ldg(slot_mapping + token);
+    if (!is_v) pos[t] = __ldg(positions + token);
+  }
 #pragma unroll
   for (int t = 0; t < kRopeTokens; ++t) {
     const int token = (int)(grp * kRopeTokens + t);
     dst_off[t] = -1;  // nothing to store
-    pos[t] = 0;
-    if (token >= num_tokens) continue;
-    int64_t slot = -1;
-    if (slot_mapping != nullptr) {
-      slot = __ldg(slot_mapping + token);
-      if (slot < -1 || slot >= num_slots) {
-        if (u == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
-        slot = -1;
-      }
+    if (token >= num_tokens || (is_v && slot_mapping == nullptr)) continue;
+    if (slot[t] < -1 || slot[t] >= num_slots) {
+      if (c == 0) record_error(VLC_DEV_ERR_SLOT_RANGE);
+      continue;
     }
-    const __nv_bfloat16* src;
-    if (is_v) {  // copied with its K row
-      if (slot < 0) continue;
-      src = value + (int64_t)token * value_stride + vh * kRopeDim;
-      dst_off[t] = slot * row_elems + vh * kRopeDim;
-    } else {
-      if (!is_q && slot_mapping != nullptr && slot < 0) continue;  // K row not stored
-      pos[t] = __ldg(positions + token);
-      if (pos[t] < 0 || pos[t] >= max_position) {
-        if (u == 0) record_error(VLC_DEV_ERR_POSITION);
-        continue;
-      }
-      src = is_q ? q + (int64_t)token * q_stride + head * kRopeDim : key + (int64_t)token * key_stride + kh * kRopeDim;
-      dst_off[t] = is_q ? (int64_t)token * q_out_stride + head * kRopeDim
-                   : slot_mapping != nullptr ? slot * row_elems + kh * kRopeDim
-                                             : (int64_t)token * k_out_stride + kh * kRopeDim;
+    if (!is_v && (pos[t] < 0 || pos[t] >= max_position)) {
+      if (c == 0) record_error(VLC_DEV_ERR_POSITION);
+      continue;
     }
-    a[t] = *reinterpret_cast<const uint4*>(src + 8 * c);
-    b[t] = *reinterpret_cast<const uint4*>(src + half + 8 * c);
+    if (is_q)
+      dst_off[t] = (int64_t)token * q_out_stride + head * kRopeDim;
+    else if (slot_mapping == nullptr)
+      dst_off[t] = is_v ? -1 : (int64_t)token * k_out_stride + kh * kRopeDim;
+    else if (slot[t] >= 0)
+      dst_off[t] = slot[t] * row_elems + (is_v ? vh : kh) * kRopeDim;
   }
 #pragma unroll
   for (int t = 0; t < kRopeTokens; ++t) {
