@@ -175,3 +175,11 @@ def test_ops_reject_cpu_tensors():
     kc = torch.zeros(2, 256, 2, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError):
         ops.store_kvcache(k, k, kc, kc, torch.zeros(4, dtype=torch.int32))
+    from vlcache_b200.layers.rotary_embedding import RotaryEmbedding
+    rot = RotaryEmbedding(128, 128, 64, 1e6)
+    pos = torch.zeros(4, dtype=torch.int64)
+    q = torch.zeros(4, 16, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        rot(pos, q, k)
+    with pytest.raises(ValueError):
+        ops.rope_store_kvcache(pos, q, k, k, rot.cos_sin_cache, kc, kc, torch.zeros(4, dtype=torch.int32))
