@@ -82,9 +82,10 @@ def causal_pairs(cu_q, cu_k):
 
 # ---------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Reads SM clocks and clock-event (throttle) reasons through NVML from a background
-    thread every ~2 ms while the timed region runs (read-only; no setting is touched).
-    Falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
+    """Reads SM clocks and clock-event (throttle) reasons through NVML (pynvml) from a
+    background thread every ~2 ms while the timed region runs (read-only; no setting is
+    touched).  NVML is the only source: without it the summary says ``"unsampled"`` and
+    reports zero samples."""
 
     REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
                ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),

@@ -44,6 +44,7 @@ extern "C" {
 #define VLC_DEV_ERR_SLOT_RANGE 101   /* slot >= num_slots or < -1 */
 #define VLC_DEV_ERR_BLOCK_RANGE 102  /* block table entry out of range where a key is needed */
 #define VLC_DEV_ERR_POSITION 103     /* rotary position outside the cos/sin cache */
+#define VLC_DEV_ERR_LENGTH 104       /* a device length exceeds the host-side bound the grid was sized for */
 #define VLC_DEV_ERR_TIMEOUT 110      /* an mbarrier wait hit its bound (base; +role id) */
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -177,7 +178,10 @@ int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num
  * at nanovllm/layers/attention.py:71-74 (one query token per sequence).
  * q: [num_seqs, num_heads, head_dim] (token stride q_seq_stride); out likewise.
  * context_lens [num_seqs] int32 on device; max_context_len is a host-side upper
- * bound used only to size the grid (graph-capture safe: no host reads).
+ * bound used only to size the grid (graph-capture safe: no host reads).  A
+ * context length above the keys that grid covers is recorded as
+ * VLC_DEV_ERR_LENGTH and only the covered keys are attended (no access outside
+ * the workspace).
  * ------------------------------------------------------------------------ */
 int vlc_decode_attn(const void* q, int64_t q_seq_stride, int num_seqs, int num_heads,
                     const void* k_cache, const void* v_cache, int64_t num_slots, int num_kv_heads,

@@ -58,6 +58,30 @@ def prefill_attention(q, k_cache, v_cache, block_tables, cu_seqlens_q, cu_seqlen
     return out
 
 
+def prefill_attention_rows(q, k_cache, v_cache, block_tables, cu_seqlens_q, cu_seqlens_k, scale: float,
+                           rows) -> torch.Tensor:
+    """The rows ``rows`` (absolute query indices) of ``prefill_attention``, computed alone:
+    row i of sequence b sees keys j <= k_len_b - q_len_b + (i - cu_q[b]), as above.  Lets a
+    test check a sample of a problem whose full fp32 evaluation would not fit the host."""
+    q = torch.as_tensor(q).float()
+    k_cache = torch.as_tensor(k_cache).float()
+    v_cache = torch.as_tensor(v_cache).float()
+    cq = np.asarray(cu_seqlens_q)
+    ck = np.asarray(cu_seqlens_k)
+    bts = np.asarray(block_tables)
+    rows = np.asarray(rows, dtype=np.int64)
+    seq = np.searchsorted(cq, rows, side="right") - 1
+    out = torch.zeros(len(rows), q.shape[1], q.shape[2])
+    for b in np.unique(seq):
+        sel = np.nonzero(seq == b)[0]
+        ql, kl = int(cq[b + 1] - cq[b]), int(ck[b + 1] - ck[b])
+        k = gather_pages(k_cache, bts[b], kl)
+        v = gather_pages(v_cache, bts[b], kl)
+        pos = torch.as_tensor(kl - ql + (rows[sel] - cq[b]))
+        out[sel] = _attend(q[rows[sel]], k, v, pos, scale)
+    return out
+
+
 def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale: float) -> torch.Tensor:
     q = torch.as_tensor(q).float()
     if q.dim() == 4:

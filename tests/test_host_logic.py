@@ -183,3 +183,24 @@ def test_ops_reject_cpu_tensors():
         rot(pos, q, k)
     with pytest.raises(ValueError):
         ops.rope_store_kvcache(pos, q, k, k, rot.cos_sin_cache, kc, kc, torch.zeros(4, dtype=torch.int32))
+
+
+def test_reuse_slot_overlap_check():
+    """Old and new block tables that share a page: rows moved onto themselves pass; a
+    destination that is another row's source (image at a different offset in the shared
+    page) is rejected before any launch."""
+    from vlcache_b200.engine import kv_cache as kvc
+    bt_old = [7, 3, 9]
+    # same image position, page 3 shared: rows in page 3 move onto themselves
+    src, dst = kvc.image_reuse_slots(20, 700, 5, [11, 3, 12], 20, bt_old)
+    kvc.check_reuse_slots(src, dst)
+    # image moved by 8 positions inside the shared page 3: slot overlap across rows
+    src, dst = kvc.image_reuse_slots(28, 708, 5, [11, 3, 12], 20, bt_old)
+    with pytest.raises(ValueError, match="overlap"):
+        kvc.check_reuse_slots(src, dst)
+    # disjoint pages: fine
+    src, dst = kvc.image_reuse_slots(28, 708, 5, [11, 13, 12], 20, bt_old)
+    kvc.check_reuse_slots(src, dst)
+    with pytest.raises(ValueError, match="overlap"):
+        kvc.copy_image_kv(torch.empty(2, 1, 16, 256, 2, 128), *kvc.image_reuse_slots(28, 708, 5, [11, 3, 12], 20,
+                                                                                        bt_old))

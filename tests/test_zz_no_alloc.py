@@ -4,14 +4,17 @@ It serves callers that may not allocate device memory (fixed memory budgets, no
 cudaMalloc after start-up): its split-K partials live in a library-owned 8 MiB device
 array instead of a caller workspace.  This file is collected last so that a run that
 stops at its first failure has already run every other test; it also passes alone.
-The check: two calls in a row with different inputs through the C ABI give the same
-result as the workspace entry point, within the attention tolerance of the other tests.
+The checks: two calls in a row with different inputs through the C ABI give the same
+result as the workspace entry point and as the fp32 CPU oracle, within the attention
+tolerance of the other tests; and once the library's device code is loaded, a call leaves
+the device's free memory unchanged (it allocates nothing).
 """
 import ctypes
 
 import pytest
 import torch
 
+from oracle import attention as oatt
 from tests.helpers import make_decode_case
 
 pytestmark = pytest.mark.gpu
@@ -40,11 +43,19 @@ def test_noalloc_decode_matches_workspace_decode_twice(cuda_lib):
         assert 0 < need <= cuda_lib.vlc_decode_noalloc_scratch_bytes()
         ref = ops.decode_attention(q, kc, vc, bt, ctx, max_len, scale)
         out = torch.full_like(ref, float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         assert _noalloc(cuda_lib, q, kc, vc, bt, ctx, max_len, scale, out) == 0
         torch.cuda.synchronize()
+        free_after = torch.cuda.mem_get_info()[0]
         assert ops.device_error() == 0
+        if seed != 21:   # the first call may load the library's device code (and its array)
+            assert free_after == free_before, (free_before, free_after)
         d = (out.float() - ref.float()).abs()
         assert torch.isfinite(out).all()
+        assert float(d.max()) <= ATT_MAX and float(d.mean()) <= ATT_MEAN
+        orc = oatt.decode_attention(q.cpu(), kc.cpu(), vc.cpu(), bt.cpu(), ctx.cpu(), scale)
+        d = (out.float().cpu() - orc).abs()
         assert float(d.max()) <= ATT_MAX and float(d.mean()) <= ATT_MEAN
 
 

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import hashlib
 import os
 import shutil
 import subprocess
@@ -45,12 +46,28 @@ def _headers() -> list[Path]:
     return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 
 
+STAMP_PATH = LIB_PATH.with_name(LIB_PATH.name + ".srchash")
+
+
+def source_hash() -> str:
+    """SHA-256 over the bytes of every source, header and this recipe (names included):
+    the library is rebuilt exactly when this differs from the hash it was built from."""
+    h = hashlib.sha256()
+    for p in _sources() + _headers() + [Path(__file__)]:
+        h.update(p.name.encode())
+        h.update(b"\0")
+        h.update(p.read_bytes())
+        h.update(b"\0")
+    return h.hexdigest()
+
+
+def is_fresh() -> bool:
+    """True when the in-tree library exists and was built from the current sources."""
+    return LIB_PATH.exists() and STAMP_PATH.exists() and STAMP_PATH.read_text().strip() == source_hash()
+
+
 def _needs_build() -> bool:
-    if not LIB_PATH.exists():
-        return True
-    t = LIB_PATH.stat().st_mtime
-    deps = _sources() + _headers() + [Path(__file__)]
-    return any(p.stat().st_mtime > t for p in deps)
+    return not is_fresh()
 
 
 def _compile(src: Path, verbose: bool) -> Path:
@@ -72,7 +89,8 @@ def _compile(src: Path, verbose: bool) -> Path:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile (if stale) and return the path of the shared library."""
+    """Compile (unless the library was built from exactly these sources) and return the
+    path of the shared library."""
     if not force and not _needs_build():
         return LIB_PATH
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
@@ -83,7 +101,9 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    digest = source_hash()
     os.replace(tmp, LIB_PATH)
+    STAMP_PATH.write_text(digest + "\n")
     return LIB_PATH
 
 

@@ -88,7 +88,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 2) decode_attn_kernel(const __gri
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_BAR + 2 * STAGES * 8);
 
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-  const int len = __ldg(p.context_lens + b);
+  int len = __ldg(p.context_lens + b);
+  // The grid (and the partials' workspace) covers max_splits * split_keys keys, the
+  // host's max_context_len rounded up: a longer device length is recorded and clamped,
+  // so no split index reaches past the partials of this sequence.
+  const int cap = p.max_splits * p.split_keys;
+  if (len > cap) {
+    if (split == 0 && g == 0 && threadIdx.x == 0) record_error(VLC_DEV_ERR_LENGTH);
+    len = cap;
+  }
   const int nsplit = len > 0 ? (len + p.split_keys - 1) / p.split_keys : 0;
   const int G = p.group;
   const int warp = warp_id(), lane = lane_id();
@@ -141,7 +149,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2) decode_attn_kernel(const __gri
           }
         }
         const int key0 = k_begin + c * CHUNK;
-        const int page = __ldg(bt + key0 / p.block_size);
+        const int pidx = key0 / p.block_size;
+        const int page = pidx < p.bt_stride ? __ldg(bt + pidx) : -1;  // past the row: recorded below
         int64_t slot = (int64_t)page * p.block_size + key0 % p.block_size;
         if (page < 0 || slot + CHUNK > p.num_slots) {
           record_error(VLC_DEV_ERR_BLOCK_RANGE);
@@ -376,7 +385,7 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (h >= num_heads) return;
-  const int len = __ldg(context_lens + b);
+  const int len = min(__ldg(context_lens + b), max_splits * split_keys);  // as clamped by the decode kernel
   const int nsplit = len > 0 ? (len + split_keys - 1) / split_keys : 0;
   if (nsplit <= 1) return;  // written directly by the decode kernel
   float M = -INFINITY;

@@ -63,14 +63,34 @@ def image_reuse_slots(img_start: int, img_end: int, num_recompute: int, new_bloc
     return src.astype(np.int32), dst.astype(np.int32)
 
 
+def check_reuse_slots(old_slots, new_slots) -> None:
+    """Raise ValueError when a slot is the source of one reused row and the destination
+    of another.  The reference's ``flat[:, :, new] = flat[:, :, old]``
+    (model_runner.py:180) reads every row before writing any; the shift kernel moves
+    row by row, which gives the same result exactly when no destination is another
+    row's source.  A row moved onto itself (a page shared by the old and the new block
+    table at the same position) is allowed."""
+    old = np.asarray(old_slots, dtype=np.int64).ravel()
+    new = np.asarray(new_slots, dtype=np.int64).ravel()
+    if old.shape != new.shape:
+        raise ValueError("old and new slot lists differ in length")
+    common, i_old, i_new = np.intersect1d(old, new, assume_unique=False, return_indices=True)
+    if len(common) and np.any(i_old != i_new):
+        bad = int(common[np.nonzero(i_old != i_new)[0][0]])
+        raise ValueError(f"reused image slots overlap: slot {bad} is the source of one row and the "
+                         "destination of another (old and new block tables share a page at "
+                         "different positions); move the rows through a fresh page first")
+
+
 def copy_image_kv(kv_cache: torch.Tensor, old_slots, new_slots, delta_thw=(0, 0, 0),
                   shift: MRopeShift | None = None) -> None:
     """Move reused image K/V rows (all layers) to new slots, rotating K by ``delta_thw``.
 
-    With a zero delta this is the reference's verbatim copy.  old and new slot sets
-    must be disjoint (they are: the new request owns freshly allocated pages)."""
+    With a zero delta this is the reference's verbatim copy.  No destination may be
+    another row's source (``check_reuse_slots``, checked here on the host lists)."""
     if len(old_slots) == 0:
         return
+    check_reuse_slots(old_slots, new_slots)
     dev = kv_cache.device
     src = torch.as_tensor(np.asarray(old_slots, dtype=np.int32)).pin_memory().to(dev, non_blocking=True)
     dst = torch.as_tensor(np.asarray(new_slots, dtype=np.int32)).pin_memory().to(dev, non_blocking=True)
@@ -79,12 +99,16 @@ def copy_image_kv(kv_cache: torch.Tensor, old_slots, new_slots, delta_thw=(0, 0,
 
 def copy_image_kv_per_layer(kv_cache: torch.Tensor, src_slots: torch.Tensor, dst_slots: torch.Tensor,
                             delta_thw=(0, 0, 0), stream: torch.cuda.Stream | None = None,
-                            shift: MRopeShift | None = None) -> list:
+                            shift: MRopeShift | None = None, check: bool = False) -> list:
     """``copy_image_kv`` as one launch per layer on ``stream`` (device int32 slot tensors),
     returning one CUDA event per layer.  Pass the events as ``set_context(..., kv_ready=...)``:
     each attention layer waits only for its own layer's rows, so the re-placement of later
     layers overlaps the compute of earlier ones.  Give ``stream`` a lower priority than
-    the compute stream (the layers' kernels then take the SMs first)."""
+    the compute stream (the layers' kernels then take the SMs first).  ``check=True`` runs
+    ``check_reuse_slots`` on a host copy of the slots first (a device read: not for
+    graph capture)."""
+    if check:
+        check_reuse_slots(src_slots.cpu().numpy(), dst_slots.cpu().numpy())
     sh = shift or MRopeShift()
     cur = torch.cuda.current_stream()
     stream = stream or cur

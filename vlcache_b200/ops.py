@@ -197,6 +197,13 @@ class PrefillPlan:
     def num_merges(self) -> int:
         return int(self.host[5])
 
+    def split_tiles(self) -> list[tuple[int, int, int]]:
+        """(first query row, query rows, KV head) of every tile whose keys are split over
+        several units (its output goes through the log-sum-exp merge of partials)."""
+        off, n = int(self.host[14]), self.num_merges
+        rec = self.host[off:off + 8 * n].reshape(n, 8) if n else np.zeros((0, 8), np.int32)
+        return [(int(r[0]), int(r[1]), int(r[2])) for r in rec]
+
 
 def build_prefill_plan(cu_seqlens_q, cu_seqlens_k, num_heads: int, num_kv_heads: int, head_dim: int = HEAD_DIM,
                        num_sms: int = 0, device: torch.device | str | None = None) -> PrefillPlan:
