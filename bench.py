@@ -15,12 +15,17 @@ Inputs are seeded N(0,1) (synthetic: no checkpoint), distinct per layer (≈0.8 
 step, larger than the 126 MB L2, so no flush is needed between steps).
 
 value  = whole-job attention TFLOP/s = N_gpus x 36 x 8.903 GFLOP / (max over ranks of the
-         device time of one step); the step is captured in a CUDA graph.
-e2e    = the same metric through the public API (``Attention.forward`` per layer) with
-         q/k/v copied from pinned host memory and the output copied back inside the timed
-         region (uploads and downloads on two copy streams, overlapping the attention).
-Also reported: attention-only µs/layer and its roofline, paged decode (
-Qwen2.5-VL-7B shapes, 256 sequences) HBM GB/s, and the CPU oracle baseline.
+         device time of one step); the step is captured in a CUDA graph.  cfg2 is one
+         request, so at N > 1 each GPU runs a replica (weak scaling).
+e2e    = the same metric through the public API with host buffers: per step the warm
+         metadata and attention plan are built and uploaded, the image rows are moved and
+         shifted, and every layer's q/k/v goes up and O comes back (``e2e_bench``).
+Also reported: attention-only µs/layer and its roofline; BASELINE config 3 (64 warm
+requests) and config 5 (256-sequence paged decode, Qwen2.5-VL-7B) with the requests dealt
+across the N GPUs (aggregate = summed work / max rank time); the config 4 ratio sweep
+(7B, 10,617 keys); config 1 (the CPU op, plus the same step on the GPU); the RoPE +
+scatter kernel; the warm metadata builder; the reference's own kernels (flash-attn) on the
+same inputs; and the CPU oracle baseline.
 
 ``--impl reference`` times the reference path's CPU restatement (fp32 torch SDPA with the
 logical-position mask, M-RoPE shift, index-copy scatter) on the host cores for a bounded
@@ -274,15 +279,31 @@ def read_profile_traffic():
 
 # ---------------------------------------------------------------------------- e2e
 def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
-    """Public API per layer (``Attention.forward``) with host buffers: H2D of each layer's
-    q/k/v from pinned memory, D2H of the attention output, all inside the timed step.
+    """One warm request end to end through the public API, every step inside the timed
+    region doing what a warm prefill does on the attention path:
 
-    The copies run on two copy streams (separate copy engines) so that layer l+1's
-    upload and layer l-1's download overlap layer l's attention; the device inputs are
-    double-buffered.  The step starts after the previous one on the compute stream and
-    the compute stream waits for the last download before the step ends."""
+      1. host: ``WarmPrefillBuilder.build_device`` lists the request's O(requests)
+         descriptors (two virtual sequences, one reused image), plans the attention kernel
+         (``vlc_prefill_plan``) and uploads descriptors, block tables, cu_seqlens and the
+         plan from pinned memory; one kernel writes positions, slot_mapping, padded block
+         tables and the image-reuse source/destination slots; ``set_context`` installs them;
+      2. the reused image rows of all 36 layers move to the request's pages with the M-RoPE
+         position shift (one launch);
+      3. per layer: q/k/v of the recomputed rows go up from pinned host memory,
+         ``Attention.forward`` scatters K/V and runs the paged prefill attention, and O comes
+         back to pinned host memory.
+
+    Uploads and downloads run on two copy streams (double-buffered inputs) and overlap the
+    attention of neighbouring layers.  Bytes counted: every host-to-device and
+    device-to-host copy of the step (q/k/v and metadata up, O down)."""
+    from vlcache_b200.engine import kv_cache as kvc
     from vlcache_b200.layers.attention import Attention
-    from vlcache_b200.utils.context import set_context
+    from vlcache_b200.layers.rotary_embedding import MRopeShift
+    from vlcache_b200.utils.context import get_context
+    req = kvc.WarmRequest(SEQLEN, list(wl.bt_new), PREFIX, PREFIX + N_IMG, R, True)
+    reuse = [kvc.ImageReuse(0, OLD_PREFIX, list(wl.bt_old))]
+    builder = kvc.WarmPrefillBuilder(H, HK)
+    shift = MRopeShift()
     host_qkv = wl.qkv.cpu().pin_memory()
     host_out = torch.empty(LAYERS, wl.total_q, H, D, dtype=torch.bfloat16).pin_memory()
     dev_qkv = [torch.empty_like(wl.qkv[0]) for _ in range(2)]
@@ -290,9 +311,7 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
     in_ready = [torch.cuda.Event() for _ in range(2)]
     in_free = [torch.cuda.Event() for _ in range(2)]
     attn = Attention(H, D, wl.scale, HK)
-    set_context(True, torch.from_numpy(wl.cu_q).to(wl.dev), torch.from_numpy(wl.cu_k).to(wl.dev),
-                int(np.diff(wl.cu_q).max()), int(np.diff(wl.cu_k).max()), wl.slot_mapping, None, wl.block_tables,
-                prefill_plan=wl.plan, cu_seqlens_q_host=wl.cu_q, cu_seqlens_k_host=wl.cu_k, workspace=wl.ws)
+    meta_bytes = [0]
 
     def upload(l):
         b = l % 2
@@ -304,11 +323,14 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
 
     def one():
         cur = torch.cuda.current_stream()
+        batch = builder.build_device([req], reuse, device=wl.dev, install=True)
+        t = batch.device_tensors
+        meta_bytes[0] = (t["descriptors"].numel() + t["cu_seqlens_q"].numel() + t["cu_seqlens_k"].numel()) * 4 + \
+            batch.plan.host.nbytes
+        get_context().workspace = wl.ws
+        shift.shift_all_layers(wl.kv_cache, t["reuse_src"], t["reuse_dst"], wl.delta)
         h2d.wait_stream(cur)
         upload(0)
-        # eager launches: the image rows of all layers move in one launch (the per-layer
-        # variant used by the graphed step costs 36 host launches here)
-        wl.ops.mrope_shift_all_layers(wl.kv_cache, wl.src, wl.dst, wl.delta)
         for l in range(LAYERS):
             b = l % 2
             if l + 1 < LAYERS:
@@ -326,7 +348,7 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
             o.record_stream(d2h)
         cur.wait_stream(d2h)
     ms = timed(one, steps, warmup, dist_on)
-    h2d_bytes = LAYERS * wl.qkv[0].numel() * 2
+    h2d_bytes = LAYERS * wl.qkv[0].numel() * 2 + meta_bytes[0]
     d2h_bytes = LAYERS * wl.total_q * H * D * 2
     return ms, h2d_bytes, d2h_bytes
 
@@ -386,17 +408,38 @@ def cfg3_requests():
     return reqs, page, n_img, R3
 
 
-def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4, impl: str = "vlcache"):
-    """Prefill attention of the cfg3 batch (3B heads) on one GPU: µs per layer and TF/s,
-    cycling through ``distinct`` layer caches (each larger than the L2), one graph;
-    ``impl="flash_attn"`` times the reference's kernel on the same data instead."""
+def cfg3_shard(rank: int = 0, world: int = 1):
+    """This rank's share of the cfg3 batch: requests dealt by attention cost (LPT,
+    vlcache_b200.engine.sharding), re-paged from 0 on this rank's own cache."""
+    from vlcache_b200.engine import kv_cache as kvc
+    from vlcache_b200.engine.sharding import attention_cost, shard_requests
+    reqs, _, _, _ = cfg3_requests()
+    costs = [attention_cost(r.img_start + r.num_recompute, r.img_start + r.num_recompute) +
+             attention_cost(r.seqlen - r.img_end, r.seqlen) for r in reqs]
+    mine = shard_requests(costs, world)[rank]
+    out, page = [], 0
+    for i in mine:
+        r = reqs[i]
+        nb = len(r.block_table)
+        out.append(kvc.WarmRequest(r.seqlen, list(range(page, page + nb)), r.img_start, r.img_end, r.num_recompute,
+                                   True))
+        page += nb
+    return out, page
+
+
+def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4, impl: str = "vlcache", rank: int = 0,
+                         world: int = 1, dist_on: bool = False):
+    """Prefill attention of this rank's share of the cfg3 batch (3B heads): µs per layer
+    and the FLOP of the share, cycling through ``distinct`` layer caches (each larger than
+    the L2), one graph; ``impl="flash_attn"`` times the reference's kernel on the same data
+    instead.  With ``dist_on`` the time is the max over ranks."""
     from vlcache_b200 import ops
     from vlcache_b200.engine import kv_cache as kvc
-    reqs, pages, _, _ = cfg3_requests()
+    reqs, pages = cfg3_shard(rank, world)
     batch = kvc.WarmPrefillBuilder(H, HK).build(reqs)
     cu_q, cu_k = batch.cu_seqlens_q, batch.cu_seqlens_k
     total_q = int(cu_q[-1])
-    g = torch.Generator(device=device).manual_seed(33)
+    g = torch.Generator(device=device).manual_seed(33 + rank)
     caches = [(torch.randn(pages, BLOCK, HK, D, generator=g, device=device).to(torch.bfloat16),
                torch.randn(pages, BLOCK, HK, D, generator=g, device=device).to(torch.bfloat16))
               for _ in range(distinct)]
@@ -424,31 +467,37 @@ def cfg3_attention_bench(device, reps: int = 20, distinct: int = 4, impl: str = 
         ms = _time_maybe_graph(layers, reps)[0] / distinct
     else:
         gr = graph_of(layers)
-        ms = timed(gr.replay, reps, 3, False) / distinct
+        ms = timed(gr.replay, reps, 3, dist_on) / distinct
+        del gr
     flop = 4 * D * H * causal_pairs(cu_q, cu_k)
     del caches
-    return {"workload": f"cfg3: 64 warm requests (3B heads), {total_q} query rows, one layer per launch",
-            "us_per_layer": ms * 1e3, "tflops": flop / (ms * 1e-3) / 1e12, "flop_per_layer": int(flop),
-            "units": plan.num_units, "split_tiles": plan.num_merges}
+    return {"requests": len(reqs), "query_rows": total_q, "us_per_layer": ms * 1e3, "flop_per_layer": int(flop),
+            "tflops": flop / (ms * 1e-3) / 1e12, "units": plan.num_units, "split_tiles": plan.num_merges}
 
 
 # ---------------------------------------------------------------------------- decode
-def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_graph=True, impl="vlcache"):
-    """cfg5 paged decode per layer; ``impl="flash_attn"`` times the reference's kernel on the
-    same data instead."""
+def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_graph=True, impl="vlcache", rank=0,
+                 world=1):
+    """cfg5 paged decode per layer over this rank's share of the 256 sequences (dealt by KV
+    length, LPT); ``impl="flash_attn"`` times the reference's kernel on the same data
+    instead.  Returns (µs per layer, GB/s of this share, bytes per layer of this share,
+    sequences); with ``dist_on`` the time is the max over ranks."""
     from vlcache_b200 import ops
+    from vlcache_b200.engine.sharding import shard_requests
     rng = np.random.default_rng(5)
-    lens = rng.integers(2700, 10701, size=DEC_SEQS)
+    lens_all = rng.integers(2700, 10701, size=DEC_SEQS)
+    lens = lens_all[shard_requests(lens_all, world)[rank]]
+    nseq = len(lens)
     nbs = (lens + BLOCK - 1) // BLOCK
     total_blocks = int(nbs.sum())
-    perm = torch.randperm(total_blocks, generator=torch.Generator().manual_seed(11)).numpy()
+    perm = torch.randperm(total_blocks, generator=torch.Generator().manual_seed(11 + rank)).numpy()
     width = int(nbs.max())
-    bt = np.full((DEC_SEQS, width), -1, np.int32)
+    bt = np.full((nseq, width), -1, np.int32)
     pos = 0
     for i, nb in enumerate(nbs):
         bt[i, :nb] = perm[pos:pos + nb]
         pos += nb
-    g = torch.Generator(device=device).manual_seed(99)
+    g = torch.Generator(device=device).manual_seed(99 + rank)
     caches = []
     for _ in range(distinct):
         kc = torch.empty(total_blocks, BLOCK, DEC_HK, D, dtype=torch.bfloat16, device=device)
@@ -456,12 +505,12 @@ def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_grap
         kc.normal_(generator=g)
         vc.normal_(generator=g)
         caches.append((kc, vc))
-    q = torch.randn(DEC_LAYERS, DEC_SEQS, DEC_H, D, generator=g, device=device).to(torch.bfloat16)
-    out = torch.empty(DEC_LAYERS, DEC_SEQS, DEC_H, D, dtype=torch.bfloat16, device=device)
+    q = torch.randn(DEC_LAYERS, nseq, DEC_H, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty(DEC_LAYERS, nseq, DEC_H, D, dtype=torch.bfloat16, device=device)
     btd = torch.from_numpy(bt).to(device)
     ctx = torch.from_numpy(lens.astype(np.int32)).to(device)
     max_len = width * BLOCK
-    ws = torch.empty(max(1, ops.decode_workspace_bytes(DEC_SEQS, DEC_H, DEC_HK, max_len)), dtype=torch.uint8,
+    ws = torch.empty(max(1, ops.decode_workspace_bytes(nseq, DEC_H, DEC_HK, max_len)), dtype=torch.uint8,
                      device=device)
     scale = 1.0 / math.sqrt(D)
 
@@ -483,12 +532,109 @@ def decode_bench(device, steps, warmup, dist_on, distinct=DEC_DISTINCT, use_grap
     elif use_graph:
         g_ = graph_of(step)
         ms = timed(g_.replay, steps, warmup, dist_on)
+        del g_
     else:
         ms = timed(step, steps, warmup, dist_on)
     bytes_per_layer = int(lens.sum()) * DEC_HK * D * 2 * 2
     us = ms * 1e3 / DEC_LAYERS
     del caches
-    return us, bytes_per_layer / (us * 1e-6) / 1e9, bytes_per_layer
+    return us, bytes_per_layer / (us * 1e-6) / 1e9, bytes_per_layer, nseq
+
+
+# ---------------------------------------------------------------------------- cfg4 / cfg1
+def cfg4_sweep(device, tf_peak, reps: int = 10, ratios=(0.02, 0.05, 0.1, 1.0)):
+    """Qwen2.5-VL-7B heads (28 / 4), one warm request with a 4K image
+    (20 + 10,549 + 48 tokens, 10,617 keys), recompute ratio swept over ``ratios``; the paged
+    prefill attention per layer, one graph of ``distinct`` layers whose K/V/Q together
+    exceed the L2 (so no flush is needed)."""
+    from vlcache_b200 import ops
+    h7, hk7 = 28, 4
+    nb = (SEQLEN + BLOCK - 1) // BLOCK
+    res = {}
+    for ratio in ratios:
+        r7 = math.ceil(ratio * N_IMG)
+        a = PREFIX + r7
+        cu_q, cu_k = np.array([0, a, a + SUFFIX], np.int32), np.array([0, a, a + SEQLEN], np.int32)
+        total_q = int(cu_q[-1])
+        layer_bytes = 2 * nb * BLOCK * hk7 * D * 2 + 2 * total_q * h7 * D * 2
+        distinct = max(1, min(8, math.ceil(160e6 / layer_bytes)))
+        g = torch.Generator(device=device).manual_seed(44)
+        kcs = [torch.randn(nb + 1, BLOCK, hk7, D, generator=g, device=device).to(torch.bfloat16)
+               for _ in range(distinct)]
+        vcs = [torch.randn(nb + 1, BLOCK, hk7, D, generator=g, device=device).to(torch.bfloat16)
+               for _ in range(distinct)]
+        qs = [torch.randn(total_q, h7, D, generator=g, device=device).to(torch.bfloat16) for _ in range(distinct)]
+        bt = torch.tensor([list(range(1, nb + 1))] * 2, dtype=torch.int32, device=device)
+        plan = ops.build_prefill_plan(cu_q, cu_k, h7, hk7, device=device)
+        ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device=device)
+        out = torch.empty(total_q, h7, D, dtype=torch.bfloat16, device=device)
+        scale = 1.0 / math.sqrt(D)
+
+        def layers():
+            for i in range(distinct):
+                ops.prefill_attention(qs[i], kcs[i], vcs[i], bt, plan, scale, out, ws)
+        gr = graph_of(layers)
+        ms = timed(gr.replay, reps, 3, False) / distinct
+        flop = 4 * D * h7 * causal_pairs(cu_q, cu_k)
+        tf = flop / (ms * 1e-3) / 1e12
+        res[str(ratio)] = {"recompute_rows": r7, "query_rows": total_q, "us_per_layer": ms * 1e3,
+                           "flop_per_layer": int(flop), "tflops": tf, "frac": tf / tf_peak,
+                           "units": plan.num_units, "split_tiles": plan.num_merges, "distinct_layers": distinct}
+        del gr, kcs, vcs, qs
+    return res
+
+
+def cfg1_bench(device, reps: int = 20):
+    """BASELINE config 1 (3B shapes, 16 + 1,024 + 32 tokens, 102 recomputed vision rows,
+    fp32, one request): the CPU op the reference defines (the oracle port: M-RoPE shift of
+    the cached vision K from offset 0 to 16, then torch SDPA with the logical-position
+    mask, on all host cores), and for comparison the same step on the GPU in bf16 through
+    this library (shift, scatter, paged prefill attention)."""
+    from oracle import attention as oatt
+    from oracle import mrope as omr
+    from tests.helpers import make_cfg1_case
+    from vlcache_b200 import ops
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    case = make_cfg1_case(dtype=torch.float32)
+    flop = 4 * D * H * causal_pairs(case.cu_q, case.cu_k)
+    c, s_ = omr.shift_table((16, 16, 16))
+    c, s_ = torch.from_numpy(c), torch.from_numpy(s_)
+    vis = case.vision_slots.long()
+
+    def cpu_step():
+        kc = case.k_cache_old.clone()
+        kr = kc.view(-1, HK, D)[vis]
+        x1, x2 = kr[..., :D // 2], kr[..., D // 2:]
+        kc.view(-1, HK, D)[vis] = torch.cat([x1 * c - x2 * s_, x2 * c + x1 * s_], -1)
+        oatt.prefill_attention(case.q, kc, case.v_cache, case.block_tables, case.cu_q, case.cu_k, case.scale)
+    for _ in range(3):
+        cpu_step()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        cpu_step()
+        ts.append(time.perf_counter() - t0)
+    cpu_us = statistics.median(ts) * 1e6
+    kc0 = case.k_cache_old.to(torch.bfloat16).to(device)
+    kc = kc0.clone()
+    vc = case.v_cache.to(torch.bfloat16).to(device)
+    q = case.q.to(torch.bfloat16).to(device)
+    bt = case.block_tables.to(device)
+    vs = case.vision_slots.to(device)
+    plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, HK, device=device)
+    out = torch.empty_like(q)
+
+    def gpu_step():
+        kc.copy_(kc0)
+        ops.mrope_shift(kc, None, vs, None, (16, 16, 16))
+        ops.prefill_attention(q, kc, vc, bt, plan, case.scale, out)
+    gr = graph_of(gpu_step)
+    ms = timed(gr.replay, reps, 3, False)
+    return {"workload": "cfg1: 3B shapes, 150 query rows x 1,072 keys, shift 16 -> fp32 CPU op",
+            "flop": int(flop), "cpu_us": cpu_us, "cpu_tflops": flop / (cpu_us * 1e-6) / 1e12, "cpu_cores": threads,
+            "cpu_kind": "port (oracle: fp32 torch shift + masked SDPA)",
+            "gpu_us": ms * 1e3, "gpu_note": "bf16, this library: cache reset copy + M-RoPE shift + attention, graphed"}
 
 
 # ---------------------------------------------------------------------------- reference kernels
@@ -562,7 +708,7 @@ def reference_kernels_bench(wl, device, reps: int = 10):
         us = ms * 1e3 / LAYERS
         res.update(prefill_us_per_layer=us, prefill_tflops=wl.flop_per_layer / (us * 1e-6) / 1e12,
                    prefill_timing=how)
-        dec_us, dec_gbs, _ = decode_bench(device, reps, 3, False, distinct=1, impl="flash_attn")
+        dec_us, dec_gbs, _, _ = decode_bench(device, reps, 3, False, distinct=1, impl="flash_attn")
         res.update(decode_us_per_layer=dec_us, decode_gbs=dec_gbs)
         c3 = cfg3_attention_bench(device, reps=reps, distinct=4, impl="flash_attn")
         res.update(cfg3_us_per_layer=c3["us_per_layer"], cfg3_tflops=c3["tflops"])
@@ -622,7 +768,8 @@ def run_only(args, device):
         c3 = cfg3_attention_bench(device, reps=max(1, args.steps), distinct=1)
         res.update(us_per_layer=c3["us_per_layer"], tflops=c3["tflops"])
     elif args.only == "decode":
-        us, gbs, nbytes = decode_bench(device, args.steps, max(3, args.warmup), False, distinct=1, use_graph=False)
+        us, gbs, nbytes, _ = decode_bench(device, args.steps, max(3, args.warmup), False, distinct=1,
+                                          use_graph=False)
         res.update(us_per_layer=us, hbm_gbs=gbs, bytes_per_layer=nbytes)
     elif args.only == "prefill_7b_full":
         # BASELINE config 4 at ratio 1.0 (7B heads, every one of the 10,617 rows recomputed):
@@ -704,6 +851,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cfg4", action="store_true", help="skip the BASELINE config 4 ratio sweep")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
     ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope"],
@@ -754,13 +902,35 @@ def main():
     ref_kernels = reference_kernels_bench(wl, device) if rank == 0 and not args.no_reference_kernels else None
     del step_graph, attn_graph, wl
     torch.cuda.empty_cache()
-    dec_us, dec_gbs, dec_bytes = decode_bench(device, args.steps, warmup, dist_on)
+
+    # Request-sharded legs (BASELINE configs 3 and 5): every rank serves its own share on its
+    # own pages; the only collectives are the timing barrier / max and these two sums.
+    c3 = cfg3_attention_bench(device, rank=rank, world=world, dist_on=dist_on)
+    dec_us, _, dec_bytes_rank, dec_seqs = decode_bench(device, args.steps, warmup, dist_on, rank=rank, world=world)
+    sums = torch.tensor([float(c3["flop_per_layer"]), float(dec_bytes_rank), float(c3["requests"]),
+                         float(dec_seqs)], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(sums)
+    c3_flop, dec_bytes, c3_reqs, dec_nseq = (float(x) for x in sums.tolist())
+    dec_gbs = dec_bytes / (dec_us * 1e-6) / 1e9
+    cfg3 = {"workload": "cfg3: 64 warm requests (3B heads, shared 1920x1080 image, ratio 0.05), requests dealt "
+                        f"to {world} GPU(s) by attention cost; one layer per launch",
+            "requests": int(c3_reqs), "flop_per_layer": int(c3_flop), "us_per_layer": c3["us_per_layer"],
+            "tflops": c3_flop / (c3["us_per_layer"] * 1e-6) / 1e12, "rank0": c3,
+            "aggregate": "sum of per-rank FLOP / max over ranks of the layer time"}
+    decode = {"workload": f"cfg5: Qwen2.5-VL-7B, 256 seqs dealt to {world} GPU(s) by KV length, "
+                          "KV len U[2700,10700], block 256",
+              "sequences": int(dec_nseq), "us_per_layer": dec_us, "hbm_gbs": dec_gbs, "frac": dec_gbs / hbm_peak,
+              "bytes_per_layer": int(dec_bytes), "peak_gbs": hbm_peak,
+              "aggregate": "sum of per-rank K/V bytes / max over ranks of the layer time"}
+
     meta = metadata_bench(device) if rank == 0 else None
-    cfg3 = cfg3_attention_bench(device) if rank == 0 else None
     rope = rope_scatter_bench(device) if rank == 0 else None
     if rope is not None:
         for r in rope.values():
             r["frac"] = r["hbm_gbs"] / hbm_peak
+    cfg4 = cfg4_sweep(device, tf_peak) if rank == 0 and not args.no_cfg4 else None
+    cfg1 = cfg1_bench(device) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -779,22 +949,27 @@ def main():
                                    "KV scatter and paged prefill attention",
                        "global_batch": world, "seq_len": SEQLEN, "query_rows": int(warm_meta()[0][-1]),
                        "keys": SEQLEN,
-                       "parallelism": f"replicas x{world}", "l2": "inputs > L2 (distinct per layer, ~0.8 GB/step)",
+                       "parallelism": f"cfg2 replicas x{world}; cfg3/cfg5 requests sharded over {world} GPU(s)",
+                       "l2": "inputs > L2 (distinct per layer, ~0.8 GB/step)",
                        "graph": "step captured in one CUDA graph"},
             "attn_us_per_layer": attn_us,
             "attn_tflops": achieved,
             "step_us_per_layer": ms_step * 1e3 / LAYERS,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": achieved / tf_peak, "peak_kind": f"bf16 burst ({peak_kind})", "traffic": traffic,
+                         "traffic_source": "from_profile: dram__bytes_read.sum + dram__bytes_write.sum per launch "
+                                           "in profiles/prefill_attn_cfg2.md (ncu), not measured in this run",
                          "frac_spec": achieved / SPEC_BF16_TFLOPS,
                          "kernel": "prefill_attn_kernel (+ split merge)",
                          "flop_per_launch": int(flop_step // LAYERS)},
-            "decode": {"workload": "cfg5: Qwen2.5-VL-7B, 256 seqs, KV len U[2700,10700], block 256",
-                       "us_per_layer": dec_us, "hbm_gbs": dec_gbs, "frac": dec_gbs / hbm_peak,
-                       "bytes_per_layer": dec_bytes, "peak_gbs": hbm_peak},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "decode": decode,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "what": "per step: host descriptors + attention plan, metadata kernel, M-RoPE shift of all "
+                            "layers, then per layer q/k/v H2D, Attention.forward, O D2H"},
             "metadata": meta,
             "cfg3_attn": cfg3,
+            "cfg4": cfg4,
+            "cfg1": cfg1,
             "rope_scatter": rope,
             "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,
