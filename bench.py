@@ -637,6 +637,73 @@ def cfg1_bench(device, reps: int = 20):
             "gpu_us": ms * 1e3, "gpu_note": "bf16, this library: cache reset copy + M-RoPE shift + attention, graphed"}
 
 
+# ---------------------------------------------------------------------------- linear layers
+def linear_bench(device, tf_peak, reps: int = 10):
+    """The recomputed rows' projections (BASELINE cfg2: 1,123 rows) on the tcgen05 GEMM, for
+    Qwen2.5-VL-3B and -7B: qkv_proj fused with bias, RoPE and the KV scatter; o_proj;
+    gate_up_proj fused with SiluAndMul; down_proj.  Each is timed against the reference's
+    own call on the same GPU and inputs (F.linear = cuBLAS, plus the separate rotary /
+    scatter / activation kernels where the fused kernel replaces them).  Weights cycle
+    through distinct copies totalling > 200 MB, so every launch reads its weights from HBM
+    as a model's layers do."""
+    import torch.nn.functional as F
+
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+    m = int(warm_meta()[0][-1])
+    table = rope_cos_sin_cache(D, 32768, 1e6).to(device)
+    res = {}
+    for model, hidden, inter, h, hk in (("3b", 2048, 11008, 16, 2), ("7b", 3584, 18944, 28, 4)):
+        g = torch.Generator(device=device).manual_seed(hidden)
+        x = torch.randn(m, hidden, generator=g, device=device).to(torch.bfloat16)
+        xi = torch.randn(m, inter, generator=g, device=device).to(torch.bfloat16)
+        pos = torch.randint(0, 32768, (m,), generator=g, device=device)
+        nb = (m + BLOCK - 1) // BLOCK + 1
+        kc = torch.zeros(nb * BLOCK, hk, D, dtype=torch.bfloat16, device=device)
+        vc = torch.zeros_like(kc)
+        slots = torch.randperm(nb * BLOCK, generator=g, device=device)[:m].to(torch.int32)
+        nq = (h + 2 * hk) * D
+        shapes = {"qkv_rope_store": (nq, hidden), "o_proj": (hidden, h * D), "gate_up_silu": (2 * inter, hidden),
+                  "down_proj": (hidden, inter)}
+        out_m = {}
+        for name, (n, k) in shapes.items():
+            distinct = max(1, min(16, math.ceil(200e6 / (n * k * 2))))
+            ws = [(torch.randn(n, k, generator=g, device=device) / math.sqrt(k)).to(torch.bfloat16)
+                  for _ in range(distinct)]
+            bias = torch.randn(n, generator=g, device=device).to(torch.bfloat16) if name == "qkv_rope_store" else None
+            a = xi if name == "down_proj" else x
+            out = torch.empty(m, n if name != "gate_up_silu" else inter, dtype=torch.bfloat16, device=device)
+
+            def ours():
+                for w in ws:
+                    if name == "qkv_rope_store":
+                        ops.qkv_rope_store_kvcache(a, w, bias, pos, table, kc, vc, slots, h, hk)
+                    elif name == "gate_up_silu":
+                        ops.linear_silu_mul(a, w, out=out)
+                    else:
+                        ops.linear(a, w, out=out)
+
+            def reference():   # the reference's calls: F.linear (+ rotary / scatter / SiluAndMul)
+                for w in ws:
+                    y = F.linear(a, w, bias)
+                    if name == "qkv_rope_store":
+                        qq, kk, vv = y.split([h * D, hk * D, hk * D], dim=-1)
+                        ops.rope_store_kvcache(pos, qq.view(m, h, D), kk.view(m, hk, D), vv.view(m, hk, D), table,
+                                               kc, vc, slots)
+                    elif name == "gate_up_silu":
+                        gg, uu = y.chunk(2, -1)
+                        F.silu(gg) * uu
+            flop = 2 * m * n * k
+            ms = timed(graph_of(ours).replay, reps, 3, False) / distinct
+            ms_ref = timed(graph_of(reference).replay, reps, 3, False) / distinct
+            tf = flop / (ms * 1e-3) / 1e12
+            out_m[name] = {"m": m, "n": n, "k": k, "us": ms * 1e3, "tflops": tf, "frac": tf / tf_peak,
+                           "cublas_path_us": ms_ref * 1e3, "speedup_vs_cublas_path": ms_ref / ms}
+            del ws
+        res[model] = out_m
+    return res
+
+
 # ---------------------------------------------------------------------------- reference kernels
 def _time_maybe_graph(fn, reps):
     """Device time of ``fn`` per call: captured in a CUDA graph when it is capture-safe,
@@ -760,7 +827,9 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "rope":
+    if args.only == "linear":
+        res["linear"] = linear_bench(device, peaks()[1], reps=max(1, args.steps))
+    elif args.only == "rope":
         # RoPE + KV scatter of the recomputed rows (cfg2 and 7B cfg4 ratio-1.0 shapes)
         res.update(rope_scatter_bench(device, reps=max(1, args.steps)))
     elif args.only == "cfg3":
@@ -854,7 +923,8 @@ def main():
     ap.add_argument("--no-cfg4", action="store_true", help="skip the BASELINE config 4 ratio sweep")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
-    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope"],
+    ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope",
+                                       "linear"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -916,11 +986,13 @@ def main():
     cfg3 = {"workload": "cfg3: 64 warm requests (3B heads, shared 1920x1080 image, ratio 0.05), requests dealt "
                         f"to {world} GPU(s) by attention cost; one layer per launch",
             "requests": int(c3_reqs), "flop_per_layer": int(c3_flop), "us_per_layer": c3["us_per_layer"],
-            "tflops": c3_flop / (c3["us_per_layer"] * 1e-6) / 1e12, "rank0": c3,
+            "tflops": c3_flop / (c3["us_per_layer"] * 1e-6) / 1e12,
+            "frac": c3_flop / (c3["us_per_layer"] * 1e-6) / 1e12 / (world * tf_peak), "rank0": c3,
             "aggregate": "sum of per-rank FLOP / max over ranks of the layer time"}
     decode = {"workload": f"cfg5: Qwen2.5-VL-7B, 256 seqs dealt to {world} GPU(s) by KV length, "
                           "KV len U[2700,10700], block 256",
-              "sequences": int(dec_nseq), "us_per_layer": dec_us, "hbm_gbs": dec_gbs, "frac": dec_gbs / hbm_peak,
+              "sequences": int(dec_nseq), "us_per_layer": dec_us, "hbm_gbs": dec_gbs,
+              "frac": dec_gbs / (world * hbm_peak), "frac_note": "aggregate GB/s / (N x measured copy peak)",
               "bytes_per_layer": int(dec_bytes), "peak_gbs": hbm_peak,
               "aggregate": "sum of per-rank K/V bytes / max over ranks of the layer time"}
 
@@ -931,6 +1003,7 @@ def main():
             r["frac"] = r["hbm_gbs"] / hbm_peak
     cfg4 = cfg4_sweep(device, tf_peak) if rank == 0 and not args.no_cfg4 else None
     cfg1 = cfg1_bench(device) if rank == 0 else None
+    lin = linear_bench(device, tf_peak) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -970,6 +1043,7 @@ def main():
             "cfg3_attn": cfg3,
             "cfg4": cfg4,
             "cfg1": cfg1,
+            "linear": lin,
             "rope_scatter": rope,
             "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,

@@ -240,6 +240,46 @@ int vlc_warm_metadata(const int32_t* vseq_desc, int num_vseqs, const int32_t* re
                       int32_t* slot_mapping, int32_t* block_tables, int block_table_width,
                       int32_t* src_slots, int32_t* dst_slots, void* stream);
 
+/* --------------------------------------------------------------------------
+ * Linear layers of the recomputed rows (tcgen05 GEMM, sm_100a).  All take
+ * x [m, k] bf16 (row stride ldx) and a weight [rows, k] bf16 (row stride ldw,
+ * nn.Linear layout), compute in fp32 and write bf16.  k, strides and output
+ * columns must be multiples of 8; pointers 16-byte aligned.
+ *
+ * vlc_linear: out[m, n] = x . weight^T (+ bias[n]).
+ *   Replaces F.linear in RowParallelLinear / ColumnParallelLinear
+ *   (nanovllm/layers/linear.py:73, :154; o_proj and down_proj of
+ *   nanovllm/models/qwen3.py:86, :116).
+ * ------------------------------------------------------------------------ */
+int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias, void* out,
+               int64_t ldo, int m, int n, int k, void* stream);
+
+/* vlc_linear_silu_mul: gate_up_weight is [2 * intermediate, k] (gate rows, then up
+ * rows, MergedColumnParallelLinear's layout); out[m, intermediate] =
+ * silu(g) * u with g, u the bf16-rounded gate / up outputs, evaluated in fp32.
+ *   Replaces gate_up_proj + SiluAndMul (nanovllm/models/qwen3.py:112-114,
+ *   nanovllm/layers/activation.py:8-14). */
+int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_up_weight, int64_t ldw, void* out,
+                        int64_t ldo, int m, int intermediate, int k, void* stream);
+
+/* vlc_qkv_rope_store_kvcache: the QKV projection of the recomputed rows with its
+ * bias, the rotary embedding and the KV scatter in one kernel.  qkv_weight is
+ * [(num_heads + 2 num_kv_heads) * head_dim, hidden] (q rows, k rows, v rows,
+ * QKVParallelLinear's layout).  Row i: qkv = bf16(x[i] . W^T + bias); q and k
+ * heads rotated at positions[i] as vlc_rope_store_kvcache does (cos_sin_cache
+ * [max_position, 128] fp32); q to q_out[i] ([m, num_heads, 128], row stride
+ * q_out_stride); k and v rows to k_cache / v_cache row slot_mapping[i] (-1:
+ * not stored; rows of num_kv_heads * 128).  head_dim must be 128.
+ *   Replaces qkv_proj -> rotary_emb -> store_kvcache
+ *   (nanovllm/models/qwen3.py:75-84, rotary_embedding.py:37-48, attention.py:10-40).
+ * Out-of-range slots / positions are recorded as VLC_DEV_ERR_SLOT_RANGE /
+ * VLC_DEV_ERR_POSITION and the row's stores skipped. */
+int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weight, int64_t ldw,
+                               const void* qkv_bias, const int64_t* positions, const float* cos_sin_cache,
+                               int64_t max_position, void* q_out, int64_t q_out_stride, void* k_cache,
+                               void* v_cache, const int32_t* slot_mapping, int64_t num_slots, int m, int hidden,
+                               int num_heads, int num_kv_heads, int head_dim, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,168 @@
+"""GPU parity of the recomputed rows' linear layers (tcgen05 GEMM, vlc_linear*).
+
+* ``vlc_linear`` against an fp32 torch reference of F.linear: every output within one
+  bf16 ulp of the fp32 result (relative 2^-7, plus 1e-2 of the output's RMS for
+  cancellation), at the BASELINE shapes (Qwen2.5-VL-3B / 7B projections of the 1,123
+  recomputed cfg2 rows) and at ragged M / N tails.
+* ``vlc_linear_silu_mul`` against silu(g) * u evaluated in fp32 from the bf16-rounded
+  gate / up outputs (SiluAndMul of nanovllm/layers/activation.py on F.linear's output).
+* ``vlc_qkv_rope_store_kvcache`` bit-exact against the same GEMM (vlc_linear with the
+  bias) followed by the RoPE + KV-scatter kernel (whose bit-exactness against the
+  reference's RotaryEmbedding is pinned by tests/test_gpu_rope.py), and within
+  tolerance of the fp32 reference path; cache rows of skipped (-1) slots untouched.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_linear(x, w, b=None):
+    y = x.float() @ w.float().t()
+    if b is not None:
+        y = y + b.float()
+    return y
+
+
+def _assert_close_ulp(out, ref, what, margins):
+    ref = ref.float()
+    d = (out.float() - ref).abs()
+    rms = float(ref.pow(2).mean().sqrt())
+    rel = d / (ref.abs() + 1e-2 * rms)
+    margins(what, float(d.max()), float(d.mean()), tol_max=float("inf"), tol_mean=float("inf"))
+    assert float(rel.max()) <= 2.0 ** -7, (what, float(rel.max()))
+
+
+@pytest.mark.parametrize("m,n,k,bias", [
+    (1123, 2560, 2048, True),     # 3B qkv_proj (cfg2 rows)
+    (1123, 2048, 2048, False),    # 3B o_proj
+    (1123, 2048, 11008, False),   # 3B down_proj
+    (1123, 4608, 3584, True),     # 7B qkv_proj
+    (1, 256, 512, False),
+    (129, 136, 64, True),         # N tail inside a 32-column chunk, M tail
+    (300, 520, 200, False),       # K not a multiple of 64
+])
+def test_linear_matches_fp32(cuda_lib, margins, m, n, k, bias):
+    from vlcache_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+    b = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16) if bias else None
+    out = ops.linear(x, w, b)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    _assert_close_ulp(out, _ref_linear(x, w, b), f"linear {m}x{n}x{k}", margins)
+
+
+def test_linear_strided_input_and_output(cuda_lib, margins):
+    """x and out as column slices of wider buffers (row strides != widths)."""
+    from vlcache_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(7)
+    xb = torch.randn(200, 1024, generator=g, device="cuda").to(torch.bfloat16)
+    x = xb[:, 64:64 + 512]
+    w = (torch.randn(384, 512, generator=g, device="cuda") / 23.0).to(torch.bfloat16)
+    ob = torch.zeros(200, 1000, dtype=torch.bfloat16, device="cuda")
+    out = ob[:, 8:8 + 384]
+    ops.linear(x, w, out=out)
+    torch.cuda.synchronize()
+    _assert_close_ulp(out, _ref_linear(x, w), "linear strided", margins)
+    assert int(ob[:, :8].abs().sum()) == 0 and int(ob[:, 392:].abs().sum()) == 0
+
+
+@pytest.mark.parametrize("m,inter,k", [(1123, 11008, 2048), (1123, 18944, 3584), (77, 200, 128)])
+def test_linear_silu_mul(cuda_lib, margins, m, inter, k):
+    from vlcache_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m + inter)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(2 * inter, k, generator=g, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+    out = ops.linear_silu_mul(x, w)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    gu = _ref_linear(x, w).to(torch.bfloat16).float()
+    gate, up = gu[:, :inter], gu[:, inter:]
+    ref = gate / (1.0 + torch.exp(-gate)) * up
+    _assert_close_ulp(out, ref, f"silu_mul {m}x{inter}x{k}", margins)
+
+
+@pytest.mark.parametrize("H,Hk,hidden", [(16, 2, 2048), (28, 4, 3584)])
+def test_qkv_rope_store_bit_exact_vs_unfused(cuda_lib, margins, H, Hk, hidden):
+    from oracle import rope as orope
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+    D, m, max_pos = 128, 1123, 16384
+    g = torch.Generator(device="cuda").manual_seed(H)
+    x = torch.randn(m, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((H + 2 * Hk) * D, hidden, generator=g, device="cuda") / math.sqrt(hidden)).to(torch.bfloat16)
+    b = torch.randn((H + 2 * Hk) * D, generator=g, device="cuda").to(torch.bfloat16)
+    table = rope_cos_sin_cache(D, max_pos, 1e6).to("cuda")
+    pos = torch.randint(0, max_pos, (m,), generator=g, device="cuda")
+    num_slots = 2048
+    slots = torch.randperm(num_slots, generator=g, device="cuda")[:m].to(torch.int32)
+    slots[::17] = -1
+    kc0 = torch.randn(num_slots, Hk, D, generator=g, device="cuda").to(torch.bfloat16)
+    vc0 = torch.randn(num_slots, Hk, D, generator=g, device="cuda").to(torch.bfloat16)
+    # fused
+    kc, vc = kc0.clone(), vc0.clone()
+    q = ops.qkv_rope_store_kvcache(x, w, b, pos, table, kc, vc, slots, H, Hk)
+    # unfused: the same GEMM, then the RoPE + scatter kernel
+    qkv = ops.linear(x, w, b)
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    q2 = ops.rope_store_kvcache(pos, qkv[:, :H * D].view(m, H, D), qkv[:, H * D:(H + Hk) * D].view(m, Hk, D),
+                                qkv[:, (H + Hk) * D:].view(m, Hk, D), table, kc2, vc2, slots)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(q.view(torch.int16), q2.view(torch.int16))
+    assert torch.equal(kc.view(torch.int16), kc2.view(torch.int16))
+    assert torch.equal(vc.view(torch.int16), vc2.view(torch.int16))
+    # rows whose slot is -1 (and slots nobody maps) keep their old contents
+    used = torch.zeros(num_slots, dtype=torch.bool, device="cuda")
+    used[slots[slots >= 0].long()] = True
+    assert torch.equal(kc[~used].view(torch.int16), kc0[~used].view(torch.int16))
+    # against the fp32 reference path (F.linear in fp32 -> bf16, oracle RoPE)
+    ref_qkv = _ref_linear(x, w, b).to(torch.bfloat16)
+    bits = lambda t: t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    sl = slots.cpu().numpy()
+    q_ref, kc_ref, vc_ref = orope.rope_store_kvcache(
+        pos.cpu().numpy(), bits(ref_qkv[:, :H * D]).reshape(m, H, D),
+        bits(ref_qkv[:, H * D:(H + Hk) * D]).reshape(m, Hk, D), bits(ref_qkv[:, (H + Hk) * D:]).reshape(m, Hk, D),
+        table.cpu().numpy(), bits(kc0).reshape(num_slots, -1), bits(vc0).reshape(num_slots, -1), sl)
+    as_f = lambda u: torch.from_numpy(u.astype(np.uint16).view(np.int16)).view(torch.bfloat16).float()  # noqa: E731
+    _assert_close_ulp(q.float().cpu(), as_f(q_ref).view(m, H, D), f"qkv_rope q (H={H})", margins)
+    _assert_close_ulp(kc.float().cpu(), as_f(kc_ref).view(num_slots, Hk, D), f"qkv_rope k cache (H={H})", margins)
+    _assert_close_ulp(vc.float().cpu(), as_f(vc_ref).view(num_slots, Hk, D), f"qkv_rope v cache (H={H})", margins)
+
+
+def test_linear_layers_dropin(cuda_lib):
+    """The layer classes load weights like the reference's (packed q/k/v and gate/up
+    shards) and their forwards equal the ops they wrap."""
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear
+    g = torch.Generator().manual_seed(5)
+    qkv = QKVParallelLinear(256, 128, 4, 2, bias=True)
+    parts = {s: torch.randn(n * 128, 256, generator=g) / 16 for s, n in (("q", 4), ("k", 2), ("v", 2))}
+    for s, t in parts.items():
+        qkv.weight.weight_loader(qkv.weight, t, s)
+        qkv.bias.weight_loader(qkv.bias, torch.randn(t.shape[0], generator=g), s)
+    assert torch.equal(qkv.weight.data, torch.cat([parts["q"], parts["k"], parts["v"]]))
+    gu = MergedColumnParallelLinear(256, [384, 384])
+    gate, up = torch.randn(384, 256, generator=g) / 16, torch.randn(384, 256, generator=g) / 16
+    gu.weight.weight_loader(gu.weight, gate, 0)
+    gu.weight.weight_loader(gu.weight, up, 1)
+    assert torch.equal(gu.weight.data, torch.cat([gate, up]))
+    down = RowParallelLinear(384, 256)
+    down.weight.weight_loader(down.weight, torch.randn(256, 384, generator=g) / 20)
+    for mod in (qkv, gu, down):
+        mod.to(device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(3, 33, 256, generator=g).to(device="cuda", dtype=torch.bfloat16)
+    y = qkv(x)
+    assert y.shape == (3, 33, 1024)
+    assert torch.equal(y.view(-1, 1024), ops.linear(x.view(-1, 256), qkv.weight, qkv.bias))
+    h = gu.forward_silu_mul(x)
+    assert h.shape == (3, 33, 384)
+    assert torch.equal(h.view(-1, 384), ops.linear_silu_mul(x.view(-1, 256), gu.weight))
+    z = down(h)
+    assert z.shape == (3, 33, 256)
+    torch.cuda.synchronize()

@@ -1,0 +1,515 @@
+// Linear layers of the recomputed rows on sm_100a: tcgen05 GEMM with TMA and TMEM.
+//
+// In a warm prefill only the recomputed rows (text + the first R vision rows) go
+// through the decoder layers, so every projection is a GEMM with a short M (cfg2:
+// 1,123 rows) and the model's weights as B:
+//   C[M, N] = A[M, K] . W[N, K]^T      (nn.Linear / F.linear, both operands K-major)
+// Replaces the reference's F.linear calls for the recomputed rows
+// (nanovllm/layers/linear.py:73, :154 via QKVParallelLinear, MergedColumnParallelLinear
+// and RowParallelLinear in nanovllm/models/qwen3.py:75-86, 112-116) with three epilogues:
+//   kPlain   : C = acc (+ bias), bf16                          (o_proj, down_proj)
+//   kSiluMul : out = silu(gate) * up over the gate and up halves of gate_up_proj's
+//              output (nanovllm/layers/activation.py SiluAndMul), bf16
+//   kQkvRope : qkv = acc + bias rounded to bf16 (the linear's output), then RoPE of the
+//              q and k heads at the row's position (rotary_embedding.py:6-14, 37-48),
+//              q to the attention input and k / v straight to their paged cache slot
+//              (store_kvcache, attention.py:10-40): the QKV projection, the rotary
+//              embedding and the KV scatter in one kernel.
+//
+// Structure: persistent CTAs (one per SM) walk output tiles of 128 x 256 in M-fastest
+// order, so the ~9 M tiles of one weight tile run side by side and share it in L2.
+//   warp 0     TMA producer: A box {64, 128} and W box {64, 256} (or two {64, 128}
+//              boxes, gate rows and up rows) per 64-wide K block into a 4-stage ring;
+//   warp 1     allocates TMEM (2 x 256 columns) and issues tcgen05.mma from one thread:
+//              4 MMAs of 128 x 256 x 16 per K block, the stage released by a commit;
+//              the accumulator of a tile alternates between the two TMEM halves;
+//   warps 2-5  epilogue: thread = TMEM lane = tile row; reads its row 32 columns at a
+//              time, applies the epilogue, stores to global memory, then releases the
+//              TMEM half so the issuer can start the tile after next in it.
+// Every mbarrier wait is bounded; a timeout records a device error and the CTA unwinds.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace vlc {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int NUM_THREADS = 192;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int NUM_BARS = 2 * STAGES + 4;  // full[S], empty[S], acc_full[2], acc_empty[2]
+constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, false, false);
+constexpr int HD = 128;  // head_dim of the QKV epilogue
+
+enum Epi : int { kPlain = 0, kSiluMul = 1, kQkvRope = 2 };
+
+struct Params {
+  CUtensorMap tm_a;  // A [M, K]: dims {K, M}, box {64, 128}
+  CUtensorMap tm_b;  // W [rows, K]: dims {K, rows}, box {64, 256} (kSiluMul: {64, 128})
+  int m, n, k;       // n = output columns (kSiluMul: the intermediate size)
+  int m_tiles, n_tiles, tiles, k_blocks;
+  int up_row0;       // kSiluMul: first W row of the up half
+  __nv_bfloat16* out;
+  int64_t ldo;
+  const __nv_bfloat16* bias;  // [n] or null (kPlain, kQkvRope)
+  // kQkvRope
+  const int64_t* positions;
+  const float* cos_sin;  // [max_position, 128]: 64 cos | 64 sin
+  int64_t max_position;
+  __nv_bfloat16* q_out;
+  int64_t q_out_stride;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  const int32_t* slot_mapping;
+  int64_t num_slots;
+  int num_heads, num_kv_heads;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int code, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > VLC_WAIT_LIMIT_CYCLES) {
+      record_error(code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 32 bf16 values (16 packed words) to 64 bytes at dst (16-byte aligned).
+__device__ __forceinline__ void store32(__nv_bfloat16* dst, const uint32_t (&w)[16]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+
+// Bias of 32 consecutive columns starting at `col` (0 when null or at columns >= n),
+// as fp32; n is a multiple of 8, so a group of 8 columns is wholly inside or outside.
+__device__ __forceinline__ void load_bias32(const __nv_bfloat16* bias, int col, int n, float (&b)[32]) {
+  if (bias == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) b[i] = 0.f;
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(bias + col);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 u = col + 8 * i < n ? __ldg(s + i) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+      b[8 * i + 2 * j] = f.x;
+      b[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = full + 2 * STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+  const int warp = warp_id(), lane = lane_id();
+
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_a);
+    tma_prefetch_desc(&p.tm_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      pdl_wait();  // A may be written by the kernel launched just before
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+        const int mt = t % p.m_tiles, nt = t / p.m_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES &&
+              !wait_bar(empty + s, (uint32_t)((it / STAGES) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 40, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + s * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_BYTES;
+          mbar_expect_tx(full + s, STAGE_BYTES);
+          tma_load_2d(a_dst, &p.tm_a, full + s, kb * BK, mt * BM);
+          if (EPI == kSiluMul) {
+            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * (BN / 2));
+            tma_load_2d(b_dst + B_BYTES / 2, &p.tm_b, full + s, kb * BK, p.up_row0 + nt * (BN / 2));
+          } else {
+            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * BN);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t base_lo = umma_desc_sw128_lo(smem_u32(smem), 16);
+      constexpr uint32_t hi = umma_desc_sw128_hi(1024);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (local >= 2 &&
+            !wait_bar(acc_empty + buf, (uint32_t)((local >> 1) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 41, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_bar(full + s, (uint32_t)(it / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 42, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_lo = base_lo + (uint32_t)((s * STAGE_BYTES) >> 4);
+          const uint32_t b_lo = a_lo + (uint32_t)(A_BYTES >> 4);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_ss_w(d, a_lo + (uint32_t)(k * 2), hi, b_lo + (uint32_t)(k * 2), hi, IDESC,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(empty + s);
+        }
+        if (!ok) break;
+        umma_commit(acc_full + buf);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2-5)
+    pdl_wait();  // positions, slots and bias may be written by the kernel launched just before
+    const int quarter = warp & 3;             // TMEM lanes [32 quarter, 32 quarter + 32)
+    const int r_in = quarter * 32 + lane;     // tile row
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    int local = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+      const int mt = t % p.m_tiles, nt = t / p.m_tiles;
+      const int buf = local & 1;
+      if (!wait_bar(acc_full + buf, (uint32_t)(local >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 43, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
+      const int row = mt * BM + r_in;
+      const bool row_ok = row < p.m;
+      if (EPI == kPlain) {
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tacc + c * 32, v);
+          tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (!row_ok || col >= p.n) continue;
+          float b[32];
+          load_bias32(p.bias, col, p.n, b);
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2(__uint_as_float(v[2 * i]) + b[2 * i], __uint_as_float(v[2 * i + 1]) + b[2 * i + 1]);
+          __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
+          if (col + 32 <= p.n) {
+            store32(dst, w);
+          } else {
+            for (int g = 0; g < 4; ++g)
+              if (col + 8 * g < p.n)
+                reinterpret_cast<uint4*>(dst)[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+          }
+        }
+      } else if (EPI == kSiluMul) {
+        // TMEM columns [0, 128): gate of output columns n0 + [0, 128); [128, 256): up.
+        const int n0 = nt * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tacc + c * 32, g);
+          tmem_ld32(tacc + BN / 2 + c * 32, u);
+          tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (!row_ok || col >= p.n) continue;
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float o[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              // gate_up_proj's output is bf16; SiluAndMul evaluates silu(x) * y in fp32
+              const float x = bf16_round(__uint_as_float(g[2 * i + e]));
+              const float y = bf16_round(__uint_as_float(u[2 * i + e]));
+              o[e] = x / (1.0f + __expf(-x)) * y;
+            }
+            w[i] = pack2(o[0], o[1]);
+          }
+          __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
+          if (col + 32 <= p.n) {
+            store32(dst, w);
+          } else {
+            for (int q = 0; q < 4; ++q)
+              if (col + 8 * q < p.n)
+                reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+        }
+      } else {
+        // kQkvRope: the tile's 256 columns are two heads of the [q | k | v] layout.
+        int64_t pos = 0, slot = -1;
+        bool pos_ok = false, slot_ok = false;
+        if (row_ok) {
+          pos = __ldg(p.positions + row);
+          slot = __ldg(p.slot_mapping + row);
+          pos_ok = pos >= 0 && pos < p.max_position;
+          slot_ok = slot >= -1 && slot < p.num_slots;
+        }
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int head = nt * 2 + hh;
+          const bool is_q = head < p.num_heads;
+          const bool is_v = head >= p.num_heads + p.num_kv_heads;
+          const int col0 = head * HD;
+          // load the head's 128 columns in two rounds of (x1: 32 of the first half,
+          // x2: the matching 32 of the second half)
+#pragma unroll 1
+          for (int r = 0; r < 2; ++r) {
+            uint32_t a[32], b[32];
+            tmem_ld32(tacc + hh * HD + r * 32, a);
+            tmem_ld32(tacc + hh * HD + 64 + r * 32, b);
+            tmem_wait_ld();
+            if (!row_ok || col0 >= p.n) continue;
+            if (!slot_ok || (!is_v && !pos_ok)) {
+              if (hh == 0 && r == 0) record_error(!slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
+              continue;
+            }
+            __nv_bfloat16* dst;
+            if (is_q) {
+              dst = p.q_out + (int64_t)row * p.q_out_stride + (int64_t)head * HD;
+            } else {
+              if (slot < 0) continue;
+              const int kvh = is_v ? head - p.num_heads - p.num_kv_heads : head - p.num_heads;
+              dst = (is_v ? p.v_cache : p.k_cache) + slot * ((int64_t)p.num_kv_heads * HD) + (int64_t)kvh * HD;
+            }
+            float bx[32], by[32];
+            load_bias32(p.bias, col0 + r * 32, p.n, bx);
+            load_bias32(p.bias, col0 + 64 + r * 32, p.n, by);
+            float x1[32], x2[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              x1[i] = bf16_round(__uint_as_float(a[i]) + bx[i]);  // the linear's bf16 output
+              x2[i] = bf16_round(__uint_as_float(b[i]) + by[i]);
+            }
+            if (!is_v) {
+              // apply_rotary_emb in fp32, each product and sum rounded on its own
+              const float* cs = p.cos_sin + pos * HD;
+#pragma unroll
+              for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + r * 32) + i4);
+                const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + 64 + r * 32) + i4);
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int i = 4 * i4 + e;
+                  const float y1 = __fsub_rn(__fmul_rn(x1[i], cv[e]), __fmul_rn(x2[i], sv[e]));
+                  const float y2 = __fadd_rn(__fmul_rn(x2[i], cv[e]), __fmul_rn(x1[i], sv[e]));
+                  x1[i] = y1;
+                  x2[i] = y2;
+                }
+              }
+            }
+            uint32_t w1[16], w2[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              w1[i] = pack2(x1[2 * i], x1[2 * i + 1]);
+              w2[i] = pack2(x2[2 * i], x2[2 * i + 1]);
+            }
+            store32(dst + r * 32, w1);
+            store32(dst + 64 + r * 32, w2);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty + buf);
+      if (*abort_flag) break;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int EPI>
+int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t w_rows, void* stream) {
+  {
+    const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)prm.m};
+    const uint64_t strides[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {BK, BM};
+    if (encode_tmap_bf16(&prm.tm_a, a, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)w_rows};
+    const uint64_t strides[1] = {(uint64_t)ldw * 2};
+    const uint32_t box[2] = {BK, (uint32_t)(EPI == kSiluMul ? BN / 2 : BN)};
+    if (encode_tmap_bf16(&prm.tm_b, w, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  }
+  prm.m_tiles = (prm.m + BM - 1) / BM;
+  prm.n_tiles = EPI == kSiluMul ? (prm.n + BN / 2 - 1) / (BN / 2) : (prm.n + BN - 1) / BN;
+  prm.tiles = prm.m_tiles * prm.n_tiles;
+  prm.k_blocks = (prm.k + BK - 1) / BK;
+  static std::atomic<uint64_t> smem_set{0};
+  if (ensure_dynamic_smem((const void*)gemm_kernel<EPI>, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
+  const int grid = std::min(prm.tiles, std::max(1, vlc_num_sms()));
+  cudaLaunchAttribute pdl;
+  pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = &pdl;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, prm) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return VLC_ERR_CUDA;
+  }
+  return VLC_OK;
+}
+
+int check_common(const void* a, int64_t lda, const void* w, int64_t ldw, int m, int k) {
+  if (!a || !w) return VLC_ERR_NULL;
+  if (m < 0 || k <= 0) return VLC_ERR_SHAPE;
+  if (lda < k || ldw < k) return VLC_ERR_STRIDE;
+  if (lda % 8 != 0 || ldw % 8 != 0 || k % 8 != 0) return VLC_ERR_STRIDE;
+  if (!aligned16(a) || !aligned16(w)) return VLC_ERR_ALIGN;
+  return VLC_OK;
+}
+
+}  // namespace gemm
+}  // namespace vlc
+
+using namespace vlc;
+using namespace vlc::gemm;
+
+extern "C" int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias, void* out,
+                          int64_t ldo, int m, int n, int k, void* stream) {
+  int rc = check_common(x, ldx, weight, ldw, m, k);
+  if (rc != VLC_OK) return rc;
+  if (!out) return VLC_ERR_NULL;
+  if (n <= 0 || n % 8 != 0) return VLC_ERR_SHAPE;
+  if (ldo < n || ldo % 8 != 0) return VLC_ERR_STRIDE;
+  if (!aligned16(out) || (bias && !aligned16(bias))) return VLC_ERR_ALIGN;
+  if (m == 0) return VLC_OK;
+  Params prm = {};
+  prm.m = m;
+  prm.n = n;
+  prm.k = k;
+  prm.out = (__nv_bfloat16*)out;
+  prm.ldo = ldo;
+  prm.bias = (const __nv_bfloat16*)bias;
+  return launch<kPlain>(prm, x, ldx, weight, ldw, n, stream);
+}
+
+extern "C" int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_up_weight, int64_t ldw, void* out,
+                                   int64_t ldo, int m, int intermediate, int k, void* stream) {
+  int rc = check_common(x, ldx, gate_up_weight, ldw, m, k);
+  if (rc != VLC_OK) return rc;
+  if (!out) return VLC_ERR_NULL;
+  if (intermediate <= 0 || intermediate % 8 != 0) return VLC_ERR_SHAPE;
+  if (ldo < intermediate || ldo % 8 != 0) return VLC_ERR_STRIDE;
+  if (!aligned16(out)) return VLC_ERR_ALIGN;
+  if (m == 0) return VLC_OK;
+  Params prm = {};
+  prm.m = m;
+  prm.n = intermediate;
+  prm.k = k;
+  prm.out = (__nv_bfloat16*)out;
+  prm.ldo = ldo;
+  prm.up_row0 = intermediate;
+  return launch<kSiluMul>(prm, x, ldx, gate_up_weight, ldw, 2LL * intermediate, stream);
+}
+
+extern "C" int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weight, int64_t ldw,
+                                          const void* qkv_bias, const int64_t* positions,
+                                          const float* cos_sin_cache, int64_t max_position, void* q_out,
+                                          int64_t q_out_stride, void* k_cache, void* v_cache,
+                                          const int32_t* slot_mapping, int64_t num_slots, int m, int hidden,
+                                          int num_heads, int num_kv_heads, int head_dim, void* stream) {
+  int rc = check_common(x, ldx, qkv_weight, ldw, m, hidden);
+  if (rc != VLC_OK) return rc;
+  if (!q_out || !k_cache || !v_cache || !slot_mapping || !positions || !cos_sin_cache) return VLC_ERR_NULL;
+  if (head_dim != HD) return VLC_ERR_UNSUPPORTED;
+  if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return VLC_ERR_SHAPE;
+  if (max_position <= 0 || num_slots <= 0) return VLC_ERR_SHAPE;
+  if (q_out_stride < (int64_t)num_heads * HD || q_out_stride % 8 != 0) return VLC_ERR_STRIDE;
+  if (!aligned16(q_out) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(cos_sin_cache) ||
+      (qkv_bias && !aligned16(qkv_bias)))
+    return VLC_ERR_ALIGN;
+  if (m == 0) return VLC_OK;
+  const int n = (num_heads + 2 * num_kv_heads) * HD;
+  Params prm = {};
+  prm.m = m;
+  prm.n = n;
+  prm.k = hidden;
+  prm.bias = (const __nv_bfloat16*)qkv_bias;
+  prm.positions = positions;
+  prm.cos_sin = cos_sin_cache;
+  prm.max_position = max_position;
+  prm.q_out = (__nv_bfloat16*)q_out;
+  prm.q_out_stride = q_out_stride;
+  prm.k_cache = (__nv_bfloat16*)k_cache;
+  prm.v_cache = (__nv_bfloat16*)v_cache;
+  prm.slot_mapping = slot_mapping;
+  prm.num_slots = num_slots;
+  prm.num_heads = num_heads;
+  prm.num_kv_heads = num_kv_heads;
+  return launch<kQkvRope>(prm, x, ldx, qkv_weight, ldw, n, stream);
+}

@@ -11,6 +11,9 @@ Optionally ``forward(q, k, v, positions=..., rotary_emb=...)`` takes q/k before 
 and rotates them in the scatter launch (vlc_rope_store_kvcache): the caller's
 ``q, k = self.rotary_emb(positions, q, k); o = self.attn(q, k, v)``
 (nanovllm/models/qwen3.py:84-86) becomes one call with the same result.
+``forward(q, None, None)`` attends over a cache that already holds this step's K/V
+(stored by ``layers.linear.QKVParallelLinear.forward_rope_store``, which fuses the
+QKV projection, RoPE and the scatter).
 """
 from __future__ import annotations
 
@@ -67,16 +70,21 @@ class Attention(nn.Module):
         self.k_cache = self.v_cache = torch.tensor([])
         self.layer_id = None  # set by engine.kv_cache.allocate_kv_cache (or the caller)
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor | None = None,
-                rotary_emb: nn.Module | None = None):
+    def forward(self, q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
+                positions: torch.Tensor | None = None, rotary_emb: nn.Module | None = None):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
+        if k is None or v is None:   # K/V already stored for this step (fused QKV projection)
+            assert k is None and v is None and rotary_emb is None
+            assert k_cache.numel() and v_cache.numel() and (context.block_tables is not None or
+                                                            not context.is_prefill), \
+                "attention without K/V reads them from the paged cache"
         if context.kv_ready is not None:    # this layer's reused rows are placed
             # (waited before the scatter: the attention kernel stays the scatter's direct
             # successor in the stream, so its programmatic launch overlaps the scatter)
             assert self.layer_id is not None, "kv_ready needs Attention.layer_id"
             torch.cuda.current_stream().wait_event(context.kv_ready[self.layer_id])
-        have_cache = bool(k_cache.numel() and v_cache.numel())
+        have_cache = bool(k_cache.numel() and v_cache.numel()) and k is not None
         if rotary_emb is not None:
             assert positions is not None, "rotary_emb needs the positions"
             if have_cache and (context.block_tables is not None or not context.is_prefill):

@@ -335,3 +335,80 @@ def warm_metadata(desc: torch.Tensor, num_vseqs: int, reuse_offset: int, num_reu
                                  _stream())
     check("vlc_warm_metadata", st)
     return positions, slots, tables, src, dst
+
+
+# --------------------------------------------------------------------------- linear layers
+def _linear_args(x: torch.Tensor, weight: torch.Tensor):
+    _require_cuda(x, weight)
+    assert x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1]
+    assert x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+    assert x.stride(1) == 1 and weight.stride(1) == 1
+    return x.shape[0], x.shape[1]
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(x, weight, bias)`` for bf16 ``x`` [m, k] and ``weight`` [n, k] on the
+    tcgen05 GEMM (nanovllm/layers/linear.py:73, :154)."""
+    m, k = _linear_args(x, weight)
+    n = weight.shape[0]
+    if bias is not None:
+        _require_cuda(bias)
+        assert bias.dtype == torch.bfloat16 and bias.is_contiguous() and bias.numel() == n
+    if out is None:
+        out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    assert out.shape == (m, n) and out.stride(1) == 1
+    st = lib().vlc_linear(_ptr(x), x.stride(0), _ptr(weight), weight.stride(0), _ptr(bias), _ptr(out),
+                          out.stride(0), m, n, k, _stream())
+    check("vlc_linear", st)
+    return out
+
+
+def linear_silu_mul(x: torch.Tensor, gate_up_weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``SiluAndMul()(F.linear(x, gate_up_weight))`` in one kernel: ``gate_up_weight`` is
+    [2 I, k] (gate rows then up rows); returns silu(gate) * up, [m, I]
+    (nanovllm/models/qwen3.py:112-114, nanovllm/layers/activation.py:8-14)."""
+    m, k = _linear_args(x, gate_up_weight)
+    assert gate_up_weight.shape[0] % 2 == 0
+    inter = gate_up_weight.shape[0] // 2
+    if out is None:
+        out = torch.empty(m, inter, dtype=x.dtype, device=x.device)
+    assert out.shape == (m, inter) and out.stride(1) == 1
+    st = lib().vlc_linear_silu_mul(_ptr(x), x.stride(0), _ptr(gate_up_weight), gate_up_weight.stride(0), _ptr(out),
+                                   out.stride(0), m, inter, k, _stream())
+    check("vlc_linear_silu_mul", st)
+    return out
+
+
+def qkv_rope_store_kvcache(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: torch.Tensor | None,
+                           positions: torch.Tensor, cos_sin_cache: torch.Tensor, k_cache: torch.Tensor,
+                           v_cache: torch.Tensor, slot_mapping: torch.Tensor, num_heads: int, num_kv_heads: int,
+                           q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """The QKV projection of the recomputed rows, its bias, the rotary embedding and the
+    KV scatter in one kernel; returns the roped q [m, num_heads, 128] and writes the
+    roped k and the v rows to the paged cache at ``slot_mapping`` (-1 skipped).
+    Same result as ``qkv = F.linear(x, W, b)``; split; ``rotary_emb(positions, q, k)``;
+    ``store_kvcache(k, v, ...)`` (nanovllm/models/qwen3.py:75-84), up to the GEMM's
+    accumulation order."""
+    m, hidden = _linear_args(x, qkv_weight)
+    D = HEAD_DIM
+    assert qkv_weight.shape[0] == (num_heads + 2 * num_kv_heads) * D
+    _require_cuda(qkv_bias, positions, cos_sin_cache, k_cache, v_cache, slot_mapping)
+    if qkv_bias is not None:
+        assert qkv_bias.dtype == torch.bfloat16 and qkv_bias.is_contiguous()
+    assert positions.dtype == torch.int64 and positions.is_contiguous() and positions.numel() == m
+    assert cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous()
+    assert cos_sin_cache.shape[-1] == D and cos_sin_cache.numel() == cos_sin_cache.shape[0] * D
+    row = num_kv_heads * D
+    assert k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.stride(1) == row
+    assert slot_mapping.dtype == torch.int32 and slot_mapping.numel() == m and slot_mapping.is_contiguous()
+    if q_out is None:
+        q_out = torch.empty(m, num_heads, D, dtype=x.dtype, device=x.device)
+    assert q_out.shape == (m, num_heads, D) and q_out.stride(2) == 1 and q_out.stride(1) == D
+    st = lib().vlc_qkv_rope_store_kvcache(_ptr(x), x.stride(0), _ptr(qkv_weight), qkv_weight.stride(0),
+                                          _ptr(qkv_bias), _ptr(positions), _ptr(cos_sin_cache),
+                                          cos_sin_cache.shape[0], _ptr(q_out), q_out.stride(0), _ptr(k_cache),
+                                          _ptr(v_cache), _ptr(slot_mapping), k_cache.numel() // row, m, hidden,
+                                          num_heads, num_kv_heads, D, _stream())
+    check("vlc_qkv_rope_store_kvcache", st)
+    return q_out
