@@ -659,7 +659,7 @@ def linear_bench(device, tf_peak, reps: int = 10):
         xi = torch.randn(m, inter, generator=g, device=device).to(torch.bfloat16)
         pos = torch.randint(0, 32768, (m,), generator=g, device=device)
         nb = (m + BLOCK - 1) // BLOCK + 1
-        kc = torch.zeros(nb * BLOCK, hk, D, dtype=torch.bfloat16, device=device)
+        kc = torch.zeros(nb, BLOCK, hk, D, dtype=torch.bfloat16, device=device)
         vc = torch.zeros_like(kc)
         slots = torch.randperm(nb * BLOCK, generator=g, device=device)[:m].to(torch.int32)
         nq = (h + 2 * hk) * D

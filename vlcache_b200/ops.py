@@ -400,7 +400,8 @@ def qkv_rope_store_kvcache(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: 
     assert cos_sin_cache.dtype == torch.float32 and cos_sin_cache.is_contiguous()
     assert cos_sin_cache.shape[-1] == D and cos_sin_cache.numel() == cos_sin_cache.shape[0] * D
     row = num_kv_heads * D
-    assert k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.stride(1) == row
+    assert k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert tuple(k_cache.shape[-2:]) == (num_kv_heads, D) and tuple(v_cache.shape) == tuple(k_cache.shape)
     assert slot_mapping.dtype == torch.int32 and slot_mapping.numel() == m and slot_mapping.is_contiguous()
     if q_out is None:
         q_out = torch.empty(m, num_heads, D, dtype=x.dtype, device=x.device)
