@@ -246,13 +246,27 @@ int vlc_warm_metadata(const int32_t* vseq_desc, int num_vseqs, const int32_t* re
  * nn.Linear layout), compute in fp32 and write bf16.  k, strides and output
  * columns must be multiples of 8; pointers 16-byte aligned.
  *
+ * Workspace (optional, all three): with workspace != NULL the K-block work may
+ * be split evenly over one CTA per SM (stream-K), which keeps every SM busy when
+ * the output has fewer 128 x 256 tiles than the GPU has SMs and each tile is
+ * long (>= 64 K blocks: down_proj of the recomputed rows); the library uses the
+ * split only there and otherwise leaves the workspace untouched.  Size: vlc_linear_workspace_size(kind,
+ * m, n, k) bytes, 256-byte aligned, ZEROED before its first use; each launch
+ * leaves it reusable (its tickets back at zero).  Launches sharing one
+ * workspace must not overlap on the GPU.  After a recorded device error, zero
+ * it again.  workspace == NULL: whole output tiles per CTA.
+ * kind: 0 vlc_linear, 1 vlc_linear_silu_mul (n = intermediate), 2 vlc_qkv_*
+ * (n = (num_heads + 2 num_kv_heads) * head_dim).
+ *
  * vlc_linear: out[m, n] = x . weight^T (+ bias[n]).
  *   Replaces F.linear in RowParallelLinear / ColumnParallelLinear
  *   (nanovllm/layers/linear.py:73, :154; o_proj and down_proj of
  *   nanovllm/models/qwen3.py:86, :116).
  * ------------------------------------------------------------------------ */
+int64_t vlc_linear_workspace_size(int kind, int m, int n, int k);
+
 int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias, void* out,
-               int64_t ldo, int m, int n, int k, void* stream);
+               int64_t ldo, int m, int n, int k, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* vlc_linear_silu_mul: gate_up_weight is [2 * intermediate, k] (gate rows, then up
  * rows, MergedColumnParallelLinear's layout); out[m, intermediate] =
@@ -260,7 +274,8 @@ int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_t ldw, cons
  *   Replaces gate_up_proj + SiluAndMul (nanovllm/models/qwen3.py:112-114,
  *   nanovllm/layers/activation.py:8-14). */
 int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_up_weight, int64_t ldw, void* out,
-                        int64_t ldo, int m, int intermediate, int k, void* stream);
+                        int64_t ldo, int m, int intermediate, int k, void* workspace, int64_t workspace_bytes,
+                        void* stream);
 
 /* vlc_qkv_rope_store_kvcache: the QKV projection of the recomputed rows with its
  * bias, the rotary embedding and the KV scatter in one kernel.  qkv_weight is
@@ -278,7 +293,8 @@ int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weigh
                                const void* qkv_bias, const int64_t* positions, const float* cos_sin_cache,
                                int64_t max_position, void* q_out, int64_t q_out_stride, void* k_cache,
                                void* v_cache, const int32_t* slot_mapping, int64_t num_slots, int m, int hidden,
-                               int num_heads, int num_kv_heads, int head_dim, void* stream);
+                               int num_heads, int num_kv_heads, int head_dim, void* workspace,
+                               int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

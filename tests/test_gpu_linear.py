@@ -67,6 +67,31 @@ def test_linear_matches_fp32(cuda_lib, margins, m, n, k, bias):
     _assert_close_ulp(out, _ref_linear(x, w, b), f"linear {m}x{n}x{k}", margins)
 
 
+@pytest.mark.parametrize("m,n,k", [(1123, 2048, 11008), (1123, 3584, 18944), (200, 512, 4096), (1, 256, 8192)])
+def test_linear_stream_k(cuda_lib, margins, m, n, k):
+    """The stream-K split (K-block ranges over one CTA per SM, partial tiles fixed up by
+    the CTA that completes them) against fp32, against whole-tile launches, run to run
+    bit-identical, and the workspace's tickets left at zero for the next launch."""
+    from vlcache_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+    b = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16)
+    sk = ops.linear(x, w, b, stream_k=True)
+    sk2 = ops.linear(x, w, b, stream_k=True)
+    whole = ops.linear(x, w, b, stream_k=False)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    ref = _ref_linear(x, w, b)
+    _assert_close_ulp(sk, ref, f"linear stream-K {m}x{n}x{k}", margins)
+    _assert_close_ulp(whole, ref, f"linear whole tiles {m}x{n}x{k}", margins)
+    assert torch.equal(sk.view(torch.int16), sk2.view(torch.int16))
+    ws, _ = ops.linear_workspace(ops.LINEAR, m, n, k, x.device)
+    tiles = -(-m // 128) * -(-n // 256)
+    off = 2 * ops.num_sms() * 128 * 256 * 4   # the tickets follow the per-SM partial slots
+    assert int(ws[off:off + 4 * tiles].view(torch.int32).abs().sum()) == 0
+
+
 def test_linear_strided_input_and_output(cuda_lib, margins):
     """x and out as column slices of wider buffers (row strides != widths)."""
     from vlcache_b200 import ops

@@ -44,10 +44,13 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_decode_noalloc_scratch_bytes": (c_i64, []),
     "vlc_warm_metadata": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_vp, c_vp,
                                   c_vp]),
-    "vlc_linear": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_int, c_int, c_int, c_vp]),
-    "vlc_linear_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_vp]),
+    "vlc_linear_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),
+    "vlc_linear": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
+    "vlc_linear_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_vp, c_i64,
+                                    c_vp]),
     "vlc_qkv_rope_store_kvcache": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp,
-                                           c_vp, c_vp, c_i64, c_int, c_int, c_int, c_int, c_int, c_vp]),
+                                           c_vp, c_vp, c_i64, c_int, c_int, c_int, c_int, c_int, c_vp, c_i64,
+                                           c_vp]),
 }
 
 

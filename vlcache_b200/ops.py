@@ -338,6 +338,32 @@ def warm_metadata(desc: torch.Tensor, num_vseqs: int, reuse_offset: int, num_reu
 
 
 # --------------------------------------------------------------------------- linear layers
+LINEAR, SILU_MUL, QKV_ROPE = 0, 1, 2
+_LINEAR_WS: dict = {}
+
+
+def linear_workspace(kind: int, m: int, n: int, k: int, device) -> tuple[torch.Tensor | None, int]:
+    """The stream-K workspace of a linear launch: one zeroed buffer per device, grown to
+    the largest size asked for (each launch leaves it zeroed; launches on one stream never
+    overlap).  Returns (tensor, bytes)."""
+    need = int(lib().vlc_linear_workspace_size(kind, m, n, k))
+    if need <= 0:
+        return None, 0
+    dev = torch.device(device)
+    key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
+    ws = _LINEAR_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        _LINEAR_WS[key] = ws
+    return ws, ws.numel()
+
+
+def reset_linear_workspaces() -> None:
+    """Zero the cached stream-K workspaces (after a recorded device error)."""
+    for ws in _LINEAR_WS.values():
+        ws.zero_()
+
+
 def _linear_args(x: torch.Tensor, weight: torch.Tensor):
     _require_cuda(x, weight)
     assert x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1]
@@ -347,9 +373,10 @@ def _linear_args(x: torch.Tensor, weight: torch.Tensor):
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-           out: torch.Tensor | None = None) -> torch.Tensor:
+           out: torch.Tensor | None = None, stream_k: bool = True) -> torch.Tensor:
     """``F.linear(x, weight, bias)`` for bf16 ``x`` [m, k] and ``weight`` [n, k] on the
-    tcgen05 GEMM (nanovllm/layers/linear.py:73, :154)."""
+    tcgen05 GEMM (nanovllm/layers/linear.py:73, :154); ``stream_k=False`` runs whole
+    output tiles per CTA (no workspace)."""
     m, k = _linear_args(x, weight)
     n = weight.shape[0]
     if bias is not None:
@@ -358,13 +385,15 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if out is None:
         out = torch.empty(m, n, dtype=x.dtype, device=x.device)
     assert out.shape == (m, n) and out.stride(1) == 1
+    ws, ws_bytes = linear_workspace(LINEAR, m, n, k, x.device) if stream_k else (None, 0)
     st = lib().vlc_linear(_ptr(x), x.stride(0), _ptr(weight), weight.stride(0), _ptr(bias), _ptr(out),
-                          out.stride(0), m, n, k, _stream())
+                          out.stride(0), m, n, k, _ptr(ws), ws_bytes, _stream())
     check("vlc_linear", st)
     return out
 
 
-def linear_silu_mul(x: torch.Tensor, gate_up_weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def linear_silu_mul(x: torch.Tensor, gate_up_weight: torch.Tensor, out: torch.Tensor | None = None,
+                    stream_k: bool = True) -> torch.Tensor:
     """``SiluAndMul()(F.linear(x, gate_up_weight))`` in one kernel: ``gate_up_weight`` is
     [2 I, k] (gate rows then up rows); returns silu(gate) * up, [m, I]
     (nanovllm/models/qwen3.py:112-114, nanovllm/layers/activation.py:8-14)."""
@@ -374,8 +403,9 @@ def linear_silu_mul(x: torch.Tensor, gate_up_weight: torch.Tensor, out: torch.Te
     if out is None:
         out = torch.empty(m, inter, dtype=x.dtype, device=x.device)
     assert out.shape == (m, inter) and out.stride(1) == 1
+    ws, ws_bytes = linear_workspace(SILU_MUL, m, inter, k, x.device) if stream_k else (None, 0)
     st = lib().vlc_linear_silu_mul(_ptr(x), x.stride(0), _ptr(gate_up_weight), gate_up_weight.stride(0), _ptr(out),
-                                   out.stride(0), m, inter, k, _stream())
+                                   out.stride(0), m, inter, k, _ptr(ws), ws_bytes, _stream())
     check("vlc_linear_silu_mul", st)
     return out
 
@@ -383,7 +413,7 @@ def linear_silu_mul(x: torch.Tensor, gate_up_weight: torch.Tensor, out: torch.Te
 def qkv_rope_store_kvcache(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: torch.Tensor | None,
                            positions: torch.Tensor, cos_sin_cache: torch.Tensor, k_cache: torch.Tensor,
                            v_cache: torch.Tensor, slot_mapping: torch.Tensor, num_heads: int, num_kv_heads: int,
-                           q_out: torch.Tensor | None = None) -> torch.Tensor:
+                           q_out: torch.Tensor | None = None, stream_k: bool = True) -> torch.Tensor:
     """The QKV projection of the recomputed rows, its bias, the rotary embedding and the
     KV scatter in one kernel; returns the roped q [m, num_heads, 128] and writes the
     roped k and the v rows to the paged cache at ``slot_mapping`` (-1 skipped).
@@ -406,10 +436,11 @@ def qkv_rope_store_kvcache(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: 
     if q_out is None:
         q_out = torch.empty(m, num_heads, D, dtype=x.dtype, device=x.device)
     assert q_out.shape == (m, num_heads, D) and q_out.stride(2) == 1 and q_out.stride(1) == D
+    ws, ws_bytes = linear_workspace(QKV_ROPE, m, qkv_weight.shape[0], hidden, x.device) if stream_k else (None, 0)
     st = lib().vlc_qkv_rope_store_kvcache(_ptr(x), x.stride(0), _ptr(qkv_weight), qkv_weight.stride(0),
                                           _ptr(qkv_bias), _ptr(positions), _ptr(cos_sin_cache),
                                           cos_sin_cache.shape[0], _ptr(q_out), q_out.stride(0), _ptr(k_cache),
                                           _ptr(v_cache), _ptr(slot_mapping), k_cache.numel() // row, m, hidden,
-                                          num_heads, num_kv_heads, D, _stream())
+                                          num_heads, num_kv_heads, D, _ptr(ws), ws_bytes, _stream())
     check("vlc_qkv_rope_store_kvcache", st)
     return q_out
