@@ -318,3 +318,32 @@ def test_device_metadata_flags_short_block_table(api):
     s = b.device_tensors["slot_mapping"].cpu().numpy()
     assert np.array_equal(s[:512], np.concatenate([np.arange(768, 1024), np.arange(1280, 1536)]))
     assert np.all(s[512:] == -1)
+
+
+def test_allocate_kv_cache_sized_from_free_memory(cuda_lib):
+    """allocate_kv_cache(num_blocks=None) sizes the pool with the reference's rule
+    (model_runner.py:130-151) and hands each Attention module its layer's K/V views and
+    layer_id (model_runner.py:152-158)."""
+    from torch import nn
+
+    from vlcache_b200.engine import kv_cache as kvc
+    from vlcache_b200.layers.attention import Attention
+
+    class Toy(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = nn.ModuleList([nn.ModuleDict({"attn": Attention(16, 128, 0.088, 2)}) for _ in range(4)])
+
+    model = Toy()
+    free, total = torch.cuda.mem_get_info()
+    util = (total - free + 3 * 2 ** 30) / total       # leave about 3 GiB to the caches
+    kv = kvc.allocate_kv_cache(model, 4, None, 2, hidden_size=2048, gpu_memory_utilization=util,
+                               encoder_cache_ratio=0.2, device="cuda")
+    b = kv.budget
+    assert kv.shape == (2, 4, b.num_kvcache_blocks, 256, 2, 128) and b.num_encoder_blocks > 0
+    assert 0.5 * 2 ** 30 < b.num_kvcache_blocks * b.kv_block_bytes <= 3 * 2 ** 30
+    for i, layer in enumerate(model.layers):
+        a = layer["attn"]
+        assert a.layer_id == i
+        assert a.k_cache.data_ptr() == kv[0, i].data_ptr() and a.v_cache.data_ptr() == kv[1, i].data_ptr()
+        assert a.k_cache.shape == (b.num_kvcache_blocks, 256, 2, 128)

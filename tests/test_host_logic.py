@@ -204,3 +204,22 @@ def test_reuse_slot_overlap_check():
     with pytest.raises(ValueError, match="overlap"):
         kvc.copy_image_kv(torch.empty(2, 1, 16, 256, 2, 128), *kvc.image_reuse_slots(28, 708, 5, [11, 3, 12], 20,
                                                                                         bt_old))
+
+
+def test_cache_budget_matches_reference_rule():
+    """The sizing rule of nanovllm/engine/model_runner.py:130-151 on fixed memory figures
+    (3B shapes: 36 layers, Hk 2, D 128, hidden 2048; a 180 GiB device)."""
+    from vlcache_b200.engine import kv_cache as kvc
+    GiB = 2 ** 30
+    total, free = 180 * GiB, 172 * GiB
+    peak, current = 9 * GiB, 7 * GiB
+    b = kvc.cache_budget(36, 2, 128, 2048, mem_info=(free, total), peak_bytes=peak, current_bytes=current,
+                         gpu_memory_utilization=0.9, encoder_cache_ratio=0.2)
+    available = total * 0.9 - (total - free) - peak + current
+    kv_block = 2 * 36 * 256 * 2 * 128 * 2
+    enc_block = 256 * 2048 * 2
+    assert b.kv_block_bytes == kv_block and b.encoder_block_bytes == enc_block
+    assert b.num_kvcache_blocks == int(available - available * 0.2) // kv_block
+    assert b.num_encoder_blocks == int(available * 0.2) // enc_block
+    with pytest.raises(ValueError):
+        kvc.cache_budget(36, 2, 128, 2048, mem_info=(1 * GiB, 180 * GiB), peak_bytes=0, current_bytes=0)

@@ -28,11 +28,71 @@ from ..utils.context import set_context
 BLOCK_SIZE = 256
 
 
-def allocate_kv_cache(model: torch.nn.Module | None, num_layers: int, num_blocks: int, num_kv_heads: int,
+@dataclass
+class CacheBudget:
+    """Block counts ``allocate_kv_cache`` derives from the device's memory, as the
+    reference's ``ModelRunner.allocate_kv_cache`` does (model_runner.py:130-151)."""
+    num_kvcache_blocks: int
+    num_encoder_blocks: int
+    kv_block_bytes: int
+    encoder_block_bytes: int
+    available_bytes: float
+
+
+def cache_budget(num_layers: int, num_kv_heads: int, head_dim: int, hidden_size: int, *, block_size: int = BLOCK_SIZE,
+                 dtype=torch.bfloat16, gpu_memory_utilization: float = 0.9, encoder_cache_ratio: float = 0.2,
+                 mem_info: tuple[int, int] | None = None, peak_bytes: int | None = None,
+                 current_bytes: int | None = None) -> CacheBudget:
+    """The reference's sizing rule (model_runner.py:130-151):
+    ``available = total * gpu_memory_utilization - used - peak + current`` (used = total -
+    free; peak / current = torch's allocated-bytes statistics), ``encoder_cache_ratio`` of
+    it for the encoder cache (blocks of ``block_size`` tokens x ``hidden_size``), the rest
+    for KV blocks of ``2 * layers * block_size * Hk * head_dim`` elements.  The memory
+    figures default to the current device's; pass them to size for another budget."""
+    if mem_info is None:
+        free, total = torch.cuda.mem_get_info()
+    else:
+        free, total = mem_info
+    if peak_bytes is None or current_bytes is None:
+        stats = torch.cuda.memory_stats()
+        peak_bytes = stats.get("allocated_bytes.all.peak", 0) if peak_bytes is None else peak_bytes
+        current_bytes = stats.get("allocated_bytes.all.current", 0) if current_bytes is None else current_bytes
+    itemsize = torch.empty((), dtype=dtype).element_size()
+    used = total - free
+    kv_block_bytes = 2 * num_layers * block_size * num_kv_heads * head_dim * itemsize
+    encoder_block_bytes = block_size * hidden_size * itemsize
+    available = total * gpu_memory_utilization - used - peak_bytes + current_bytes
+    encoder_memory = available * encoder_cache_ratio
+    kv_memory = available - encoder_memory
+    budget = CacheBudget(int(kv_memory) // kv_block_bytes, int(encoder_memory) // encoder_block_bytes,
+                         kv_block_bytes, encoder_block_bytes, available)
+    if budget.num_kvcache_blocks <= 0:
+        raise ValueError(f"no memory left for KV blocks ({available / 2**30:.2f} GiB available)")
+    return budget
+
+
+def allocate_kv_cache(model: torch.nn.Module | None, num_layers: int, num_blocks: int | None, num_kv_heads: int,
                       head_dim: int = 128, block_size: int = BLOCK_SIZE, dtype=torch.bfloat16,
-                      device="cuda") -> torch.Tensor:
+                      device="cuda", *, hidden_size: int | None = None, gpu_memory_utilization: float = 0.9,
+                      encoder_cache_ratio: float = 0.2) -> torch.Tensor:
+    """``[2, L, num_blocks, block_size, Hk, D]`` with per-layer views handed to every module
+    that has ``k_cache`` / ``v_cache`` (model_runner.py:152-158), plus the module's
+    ``layer_id``.  ``num_blocks=None`` sizes the pool from the device's free memory with
+    the reference's rule (``cache_budget``, which needs ``hidden_size`` for the encoder
+    cache share); the tensor's ``budget`` attribute then holds the block counts, the
+    encoder-cache block count included."""
+    budget = None
+    if num_blocks is None:
+        if hidden_size is None:
+            raise ValueError("sizing from free memory needs hidden_size (the encoder cache's share)")
+        with torch.cuda.device(torch.device(device)):
+            budget = cache_budget(num_layers, num_kv_heads, head_dim, hidden_size, block_size=block_size, dtype=dtype,
+                                  gpu_memory_utilization=gpu_memory_utilization,
+                                  encoder_cache_ratio=encoder_cache_ratio)
+        num_blocks = budget.num_kvcache_blocks
     kv_cache = torch.empty(2, num_layers, num_blocks, block_size, num_kv_heads, head_dim, dtype=dtype,
                            device=device)
+    kv_cache.budget = budget
     if model is not None:
         layer_id = 0
         for module in model.modules():
