@@ -704,6 +704,54 @@ def linear_bench(device, tf_peak, reps: int = 10):
     return res
 
 
+# ---------------------------------------------------------------------------- encoder-cache hash
+def encoder_hash_bench(device, hbm_peak, reps: int = 20):
+    """Key of one 4K image for the encoder cache (42,196 patches x 1,176 fp32 = 198 MB):
+    this library's tree hash on the GPU (pixels resident in HBM) and on all host threads,
+    against the reference's compute_hash (nanovllm/engine/encoder_cache_manager.py:24-29:
+    ``.cpu()`` of the tensor, then xxhash.xxh64 over grid_thw and pixel bytes)."""
+    from vlcache_b200 import ops
+    g = torch.Generator(device=device).manual_seed(4)
+    px = torch.randn(42196, 1176, generator=g, device=device)
+    header = np.array([1, 154, 274], np.int64).tobytes()
+    nbytes = px.numel() * 4
+    ws = torch.empty(int(ops.lib().vlc_content_hash_workspace_size(nbytes)), dtype=torch.uint8, device=device)
+
+    def dev():
+        ops.content_hash_device_async(px, header, ws)
+    us_dev = timed(graph_of(dev).replay, reps, 3, False) * 1e3
+    host = px.cpu()
+    threads = os.cpu_count() or 1
+    ts = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        ops.content_hash(host, header)
+        ts.append(time.perf_counter() - t0)
+    ms_host = statistics.median(ts) * 1e3
+    res = {"workload": "4K image pixels: 42,196 x 1,176 fp32 (198 MB) + grid_thw header",
+           "bytes": nbytes, "gpu_us": us_dev, "gpu_gbs": nbytes / (us_dev * 1e-6) / 1e9,
+           "gpu_frac": nbytes / (us_dev * 1e-6) / 1e9 / hbm_peak, "host_tree_ms": ms_host, "host_threads": threads}
+    try:
+        import xxhash
+
+        def reference():   # the reference's compute_hash on the device tensor
+            h = xxhash.xxh64()
+            h.update(torch.tensor([1, 154, 274]).cpu().numpy().tobytes())
+            h.update(px.cpu().numpy().tobytes())
+            return h.intdigest()
+        ts = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            reference()
+            ts.append(time.perf_counter() - t0)
+        res["reference_ms"] = statistics.median(ts) * 1e3
+        res["speedup_gpu_vs_reference"] = res["reference_ms"] * 1e3 / us_dev
+    except ImportError:
+        res["reference_ms"] = None
+    del px, host
+    return res
+
+
 # ---------------------------------------------------------------------------- reference kernels
 def _time_maybe_graph(fn, reps):
     """Device time of ``fn`` per call: captured in a CUDA graph when it is capture-safe,
@@ -827,7 +875,9 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "linear":
+    if args.only == "hash":
+        res["encoder_hash"] = encoder_hash_bench(device, peaks()[0], reps=max(1, args.steps))
+    elif args.only == "linear":
         res["linear"] = linear_bench(device, peaks()[1], reps=max(1, args.steps))
     elif args.only == "rope":
         # RoPE + KV scatter of the recomputed rows (cfg2 and 7B cfg4 ratio-1.0 shapes)
@@ -924,7 +974,7 @@ def main():
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
     ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope",
-                                       "linear"],
+                                       "linear", "hash"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1004,6 +1054,7 @@ def main():
     cfg4 = cfg4_sweep(device, tf_peak) if rank == 0 and not args.no_cfg4 else None
     cfg1 = cfg1_bench(device) if rank == 0 else None
     lin = linear_bench(device, tf_peak) if rank == 0 else None
+    ehash = encoder_hash_bench(device, hbm_peak) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1044,6 +1095,7 @@ def main():
             "cfg4": cfg4,
             "cfg1": cfg1,
             "linear": lin,
+            "encoder_hash": ehash,
             "rope_scatter": rope,
             "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,

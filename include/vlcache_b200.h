@@ -296,6 +296,30 @@ int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weigh
                                int num_heads, int num_kv_heads, int head_dim, void* workspace,
                                int64_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------------------------------
+ * Content hash of encoder-cache inputs.  Replaces EncoderCacheManager.compute_hash
+ * (nanovllm/engine/encoder_cache_manager.py:24-29: XXH64 of grid_thw bytes then
+ * pixel bytes, on the host, called per image at nanovllm/engine/llm_engine.py:52)
+ * with a tree of XXH64 whose leaves hash in parallel (same bytes -> same key):
+ *   d1[i] = XXH64(data[1024 i, 1024 (i+1)), seed 1)      (last chunk shorter)
+ *   d2[j] = XXH64(d1 as little-endian bytes [1024 j, 1024 (j+1)), seed 2)
+ *   digest = XXH64(little-endian uint64 words {header_len, header zero-padded to a
+ *            multiple of 8 bytes, nbytes, n1 = #d1, d2...}, seed 3)
+ * header: the caller's bytes (e.g. grid_thw as int64 x 3), at most 256.
+ *
+ * vlc_content_hash_device: data in device memory; digest (one uint64) written to
+ *   device memory `digest` on `stream` (two launches); workspace of
+ *   vlc_content_hash_workspace_size(nbytes) bytes, 8-byte aligned.
+ * vlc_content_hash_host: data in host memory, level 1 split over num_threads
+ *   threads (<= 0: all hardware threads); digest written to *digest.
+ * vlc_xxh64: plain XXH64 of a host buffer (the tree's primitive). */
+int64_t vlc_content_hash_workspace_size(int64_t nbytes);
+int vlc_content_hash_device(const void* data, int64_t nbytes, const void* header, int header_bytes, void* workspace,
+                            int64_t workspace_bytes, uint64_t* digest, void* stream);
+int vlc_content_hash_host(const void* data, int64_t nbytes, const void* header, int header_bytes, int num_threads,
+                          uint64_t* digest);
+uint64_t vlc_xxh64(const void* data, int64_t nbytes, uint64_t seed);
+
 #ifdef __cplusplus
 }
 #endif

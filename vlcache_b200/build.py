@@ -27,7 +27,7 @@ BUILD_DIR = REPO_DIR / "_build" / "vlcache_b200"
 LIB_PATH = PKG_DIR / "libvlcache_b200.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["runtime.cu", "kv_ops.cu", "prefill_attn.cu", "decode_attn.cu", "metadata.cu", "gemm.cu"]
+CUDA_SOURCES = ["runtime.cu", "kv_ops.cu", "prefill_attn.cu", "decode_attn.cu", "metadata.cu", "gemm.cu", "content_hash.cu"]
 CPP_SOURCES = ["plan.cpp"]
 
 

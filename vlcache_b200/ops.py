@@ -444,3 +444,49 @@ def qkv_rope_store_kvcache(x: torch.Tensor, qkv_weight: torch.Tensor, qkv_bias: 
                                           num_heads, num_kv_heads, D, _ptr(ws), ws_bytes, _stream())
     check("vlc_qkv_rope_store_kvcache", st)
     return q_out
+
+
+# --------------------------------------------------------------------------- content hash
+def _header_buf(header: bytes):
+    hb = bytes(header)
+    return ctypes.create_string_buffer(hb, max(1, len(hb))), len(hb)
+
+
+def content_hash_device_async(data: torch.Tensor, header: bytes = b"",
+                              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Tree-XXH64 digest (include/vlcache_b200.h, vlc_content_hash_*) of a CUDA tensor's
+    bytes with ``header``, as a one-element int64 device tensor (the uint64 bit pattern),
+    computed on the current stream without any host synchronisation."""
+    _require_cuda(data)
+    assert data.is_contiguous(), "hash a contiguous tensor"
+    nbytes = data.numel() * data.element_size()
+    need = int(lib().vlc_content_hash_workspace_size(nbytes))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=data.device)
+    out = torch.empty(1, dtype=torch.int64, device=data.device)
+    hb, hl = _header_buf(header)
+    st = lib().vlc_content_hash_device(_ptr(data), nbytes, hb, hl, _ptr(workspace),
+                                       workspace.numel() * workspace.element_size(), _ptr(out), _stream())
+    check("vlc_content_hash_device", st)
+    return out
+
+
+def content_hash(data: torch.Tensor | np.ndarray, header: bytes = b"", num_threads: int = 0) -> int:
+    """Tree-XXH64 digest of a tensor's bytes as a Python int: on the GPU when the tensor
+    lives there (one 8-byte read back), else on the host threads."""
+    if torch.is_tensor(data) and data.is_cuda:
+        return int(content_hash_device_async(data, header).item()) & (2 ** 64 - 1)
+    arr = np.ascontiguousarray(data.numpy() if torch.is_tensor(data) else data)
+    hb, hl = _header_buf(header)
+    out = ctypes.c_uint64(0)
+    st = lib().vlc_content_hash_host(ctypes.c_void_p(arr.ctypes.data), arr.nbytes, hb, hl, num_threads,
+                                     ctypes.byref(out))
+    check("vlc_content_hash_host", st)
+    return int(out.value)
+
+
+def xxh64(data: bytes | np.ndarray, seed: int = 0) -> int:
+    """Plain XXH64 of host bytes (the tree's primitive)."""
+    arr = np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) else \
+        np.ascontiguousarray(data).reshape(-1).view(np.uint8)
+    return int(lib().vlc_xxh64(ctypes.c_void_p(arr.ctypes.data if arr.size else 0), arr.size, seed))
