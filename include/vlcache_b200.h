@@ -308,8 +308,8 @@ int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weigh
  * header: the caller's bytes (e.g. grid_thw as int64 x 3), at most 256.
  *
  * vlc_content_hash_device: data in device memory; digest (one uint64) written to
- *   device memory `digest` on `stream` (two launches); workspace of
- *   vlc_content_hash_workspace_size(nbytes) bytes, 8-byte aligned.
+ *   device memory `digest` on `stream` (three launches); workspace of
+ *   vlc_content_hash_workspace_size(nbytes) bytes, 16-byte aligned.
  * vlc_content_hash_host: data in host memory, level 1 split over num_threads
  *   threads (<= 0: all hardware threads); digest written to *digest.
  * vlc_xxh64: plain XXH64 of a host buffer (the tree's primitive). */

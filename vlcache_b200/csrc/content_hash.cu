@@ -180,20 +180,41 @@ struct Header {
   int len;
 };
 
-// Level 2 + the digest, one block: thread j hashes level-2 chunk j (128 level-1
-// digests) into the final word stream in shared memory, then thread 0 hashes the stream.
-constexpr int kFinalThreads = 1024;
+// Level 2: thread j hashes level-2 chunk j, i.e. 128 level-1 digests (fewer in the
+// last), as 64-bit words with 16-byte loads: XXH64 of 8k bytes is xxh64_words of k words.
+__global__ void __launch_bounds__(256) hash_level2_kernel(const uint64_t* __restrict__ d1, int64_t n1,
+                                                          uint64_t* __restrict__ d2, int64_t n2) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n2) return;
+  const int64_t w0 = j * (kChunk / 8);
+  const int64_t cnt = min((int64_t)(kChunk / 8), n1 - w0);
+  if (cnt < kChunk / 8) {
+    d2[j] = xxh64_words(d1 + w0, cnt, 2);
+    return;
+  }
+  uint64_t v1 = 2 + P1 + P2, v2 = 2 + P2, v3 = 2, v4 = 2 - P1;
+  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(d1 + w0);
+#pragma unroll 4
+  for (int s = 0; s < kChunk / 32; ++s) {
+    const ulonglong2 a = q[2 * s], b = q[2 * s + 1];
+    v1 = xround(v1, a.x);
+    v2 = xround(v2, a.y);
+    v3 = xround(v3, b.x);
+    v4 = xround(v4, b.y);
+  }
+  d2[j] = avalanche(xstripes_done(v1, v2, v3, v4) + (uint64_t)kChunk);
+}
+
+// The digest, one block: the final word stream is gathered in shared memory (the level-2
+// digests copied by all threads), then thread 0 hashes it.
+constexpr int kFinalThreads = 256;
 constexpr int kFinalSmemMax = 200 * 1024;
-__global__ void __launch_bounds__(kFinalThreads) hash_final_kernel(const uint64_t* __restrict__ d1, int64_t n1,
-                                                                   int64_t nbytes, const __grid_constant__ Header hdr,
-                                                                   uint64_t* out) {
+__global__ void __launch_bounds__(kFinalThreads) hash_final_kernel(const uint64_t* __restrict__ d2, int64_t n2,
+                                                                   int64_t n1, int64_t nbytes,
+                                                                   const __grid_constant__ Header hdr, uint64_t* out) {
   extern __shared__ uint64_t words[];  // [1 + header words + 2 + n2]
   const int hw = (hdr.len + 7) / 8;
-  const int64_t bytes1 = n1 * 8;
-  const int64_t n2 = (bytes1 + kChunk - 1) / kChunk;
-  uint64_t* d2 = words + 3 + hw;
-  for (int64_t j = threadIdx.x; j < n2; j += blockDim.x)
-    d2[j] = xxh64(reinterpret_cast<const uint8_t*>(d1) + j * kChunk, min(kChunk, bytes1 - j * kChunk), 2);
+  for (int64_t j = threadIdx.x; j < n2; j += blockDim.x) words[3 + hw + j] = d2[j];
   if (threadIdx.x == 0) {
     words[0] = (uint64_t)hdr.len;
     for (int k = 0; k < hw; ++k) {
@@ -236,7 +257,8 @@ using namespace vlc::chash;
 
 extern "C" int64_t vlc_content_hash_workspace_size(int64_t nbytes) {
   if (nbytes < 0) return -1;
-  return std::max<int64_t>(1, level1_chunks(nbytes)) * 8;  // the level-1 digests
+  const int64_t n1 = level1_chunks(nbytes);
+  return std::max<int64_t>(1, n1 + level2_chunks(n1)) * 8;  // the level-1 and level-2 digests
 }
 
 extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const void* header, int header_bytes,
@@ -245,19 +267,23 @@ extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const v
   if (header_bytes > kMaxHeader) return VLC_ERR_UNSUPPORTED;
   if ((nbytes > 0 && !data) || (header_bytes > 0 && !header) || !digest || !workspace) return VLC_ERR_NULL;
   if (workspace_bytes < vlc_content_hash_workspace_size(nbytes)) return VLC_ERR_WORKSPACE;
-  if ((uintptr_t)workspace % 8 != 0 || (uintptr_t)digest % 8 != 0) return VLC_ERR_ALIGN;
+  if ((uintptr_t)workspace % 16 != 0 || (uintptr_t)digest % 8 != 0) return VLC_ERR_ALIGN;
   const int64_t n1 = level1_chunks(nbytes);
   const int64_t n2 = level2_chunks(n1);
   const int64_t final_smem = (3 + (header_bytes + 7) / 8 + n2) * 8;
   if (final_smem > kFinalSmemMax) return VLC_ERR_UNSUPPORTED;  // inputs above about 3 TB
   uint64_t* d1 = (uint64_t*)workspace;
+  uint64_t* d2 = d1 + n1;  // 16-byte aligned chunks of d1 (1,024 bytes each)
   cudaStream_t st = (cudaStream_t)stream;
   if (n1 > 0) {
     const int64_t blocks = (n1 + 255) / 256;
     if (blocks > 0x7fffffff) return VLC_ERR_SHAPE;
     hash_chunks_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint8_t*)data, nbytes, d1, n1, 1,
                                                          aligned16(data) ? 1 : 0);
-    const int rc = launch_status();
+    int rc = launch_status();
+    if (rc != VLC_OK) return rc;
+    hash_level2_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(d1, n1, d2, n2);
+    rc = launch_status();
     if (rc != VLC_OK) return rc;
   }
   Header h;
@@ -266,7 +292,7 @@ extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const v
   h.len = header_bytes;
   static std::atomic<uint64_t> smem_set{0};
   if (ensure_dynamic_smem((const void*)hash_final_kernel, kFinalSmemMax, smem_set) != VLC_OK) return VLC_ERR_CUDA;
-  hash_final_kernel<<<1, kFinalThreads, (size_t)final_smem, st>>>(d1, n1, nbytes, h, digest);
+  hash_final_kernel<<<1, kFinalThreads, (size_t)final_smem, st>>>(d2, n2, n1, nbytes, h, digest);
   return launch_status();
 }
 
