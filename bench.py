@@ -752,6 +752,55 @@ def encoder_hash_bench(device, hbm_peak, reps: int = 20):
     return res
 
 
+# ---------------------------------------------------------------------------- vision attention
+def vision_attention_bench(device, tf_peak, reps: int = 5):
+    """The vision tower's attention for one 4K image (77 x 137 merged grid, 42,196
+    patches, 16 heads of 80; nanovllm/models/qwen2_5_vl.py:202-211): a window block
+    (windows of 4 x 4 merged tokens = 64 patches, ragged at the borders) and a
+    full-attention block, non-causal, on the tcgen05 kernel and on flash-attn (the
+    reference's call) with the same inputs.  FLOP = 4 x 80 x 16 x sum of q.k pairs."""
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.vision_attention import plan_varlen
+    gh, gw, H, d = 77, 137, 16, 80
+    wl = []
+    for r0 in range(0, gh, 4):
+        for c0 in range(0, gw, 4):
+            wl.append(min(4, gh - r0) * min(4, gw - c0) * 4)
+    n = gh * gw * 4
+    g = torch.Generator(device=device).manual_seed(8)
+    qkv = torch.randn(n, 3, H, d, generator=g, device=device).to(torch.bfloat16)
+    q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+    out = torch.empty(n, H, d, dtype=torch.bfloat16, device=device)
+    scale = 1.0 / math.sqrt(d)
+    res = {"workload": "4K image vision tower: 42,196 patches, 16 heads x 80, non-causal"}
+    try:
+        import flash_attn as fa
+    except Exception:  # noqa: BLE001
+        fa = None
+    for name, lens in (("window_block", wl), ("full_block", [n])):
+        cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+        cu_d = torch.from_numpy(cu).to(device)
+        plan = plan_varlen(cu, cu, H, H, d, causal=False, device=device)
+        ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device=device)
+        flop = 4 * d * H * int(sum(x * x for x in lens))
+
+        def ours():
+            ops.prefill_attention(q, k, v, None, plan, scale, out, ws)
+        ms = timed(graph_of(ours).replay, reps, 2, False)
+        r = {"windows": len(lens), "us": ms * 1e3, "tflops": flop / (ms * 1e-3) / 1e12,
+             "frac": flop / (ms * 1e-3) / 1e12 / tf_peak, "flop": flop}
+        if fa is not None:
+            mx = int(max(lens))
+
+            def ref():
+                fa.flash_attn_varlen_func(q, k, v, cu_d, cu_d, mx, mx, softmax_scale=scale, causal=False)
+            ms_fa, how = _time_maybe_graph(ref, reps)
+            r.update(flash_attn_us=ms_fa * 1e3, speedup_vs_flash_attn=ms_fa / ms)
+        res[name] = r
+    del qkv, out
+    return res
+
+
 # ---------------------------------------------------------------------------- reference kernels
 def _time_maybe_graph(fn, reps):
     """Device time of ``fn`` per call: captured in a CUDA graph when it is capture-safe,
@@ -875,7 +924,9 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "hash":
+    if args.only == "vision":
+        res["vision_attention"] = vision_attention_bench(device, peaks()[1], reps=max(1, args.steps))
+    elif args.only == "hash":
         res["encoder_hash"] = encoder_hash_bench(device, peaks()[0], reps=max(1, args.steps))
     elif args.only == "linear":
         res["linear"] = linear_bench(device, peaks()[1], reps=max(1, args.steps))
@@ -974,7 +1025,7 @@ def main():
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
     ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope",
-                                       "linear", "hash"],
+                                       "linear", "hash", "vision"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1055,6 +1106,7 @@ def main():
     cfg1 = cfg1_bench(device) if rank == 0 else None
     lin = linear_bench(device, tf_peak) if rank == 0 else None
     ehash = encoder_hash_bench(device, hbm_peak) if rank == 0 else None
+    vit = vision_attention_bench(device, tf_peak) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1096,6 +1148,7 @@ def main():
             "cfg1": cfg1,
             "linear": lin,
             "encoder_hash": ehash,
+            "vision_attention": vit,
             "rope_scatter": rope,
             "reference_kernels": ref_kernels,
             "gpu_launches": launches * args.steps,

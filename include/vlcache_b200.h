@@ -137,6 +137,18 @@ int vlc_prefill_plan(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, i
 int64_t vlc_prefill_plan_capacity(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
                                   int num_seqs, int num_heads, int num_kv_heads, int num_sms);
 
+/* The same plan for the general varlen attention: causal != 0 is vlc_prefill_plan;
+ * causal == 0 lets every query row of a sequence see all k_len keys of it, as
+ * flash_attn_varlen_func(..., causal=False) in the vision tower's window and full
+ * attention (nanovllm/models/qwen2_5_vl.py:202-211).  head_dim: 64 < d <= 128,
+ * a multiple of 16 (Qwen2.5-VL's vision heads: 80).  vlc_prefill_plan(...) equals
+ * vlc_attention_plan(..., causal = 1, ...). */
+int vlc_attention_plan(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs, int num_heads,
+                       int num_kv_heads, int head_dim, int causal, int num_sms, int32_t* plan_out,
+                       int64_t plan_capacity, int64_t* plan_len);
+int64_t vlc_attention_plan_capacity(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs,
+                                    int num_heads, int num_kv_heads, int causal, int num_sms);
+
 /* Workspace bytes vlc_prefill_attn needs for a given (host) plan. */
 int64_t vlc_prefill_workspace_size(const int32_t* plan_host);
 
@@ -157,7 +169,9 @@ int64_t vlc_prefill_workspace_size(const int32_t* plan_host);
  * plan_dev is the plan from vlc_prefill_plan copied to device memory;
  * plan_host is the same plan on the host (only its header is read).
  * out: [total_q, num_heads, head_dim] bf16 with token stride out_token_stride.
- * head_dim must be 128.
+ * head_dim: 64 < d <= 128, a multiple of 16, equal to the plan's (q/k/v tiles are
+ * zero-padded to 128 columns on load; outputs are written for the d real ones).
+ * The plan's causal flag selects the mask (vlc_attention_plan).
  * Launch order: the attention is a programmatic dependent launch of the kernel
  * enqueued just before it on `stream` (its setup overlaps that kernel's tail).
  * That kernel may write q, k and v; plan_dev and block_tables must have been

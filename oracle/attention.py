@@ -39,6 +39,26 @@ def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tens
     return torch.bmm(p, vv).permute(1, 0, 2)              # [Nq, H, D]
 
 
+def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale: float, causal: bool = False) -> torch.Tensor:
+    """``flash_attn_varlen_func`` on contiguous-by-token q [total_q, H, d] and k / v
+    [total_k, Hk, d]: sequence b's rows attend to its keys, every key when not causal (the
+    vision tower's window and full attention, nanovllm/models/qwen2_5_vl.py:202-211),
+    bottom-right causal otherwise.  fp32."""
+    q = torch.as_tensor(q).float()
+    k = torch.as_tensor(k).float()
+    v = torch.as_tensor(v).float()
+    cq = np.asarray(cu_seqlens_q)
+    ck = np.asarray(cu_seqlens_k)
+    out = torch.zeros_like(q)
+    for b in range(len(cq) - 1):
+        ql, kl = int(cq[b + 1] - cq[b]), int(ck[b + 1] - ck[b])
+        if ql == 0:
+            continue
+        pos = torch.arange(kl - ql, kl) if causal else torch.full((ql,), kl - 1)
+        out[cq[b]:cq[b + 1]] = _attend(q[cq[b]:cq[b + 1]], k[ck[b]:ck[b + 1]], v[ck[b]:ck[b + 1]], pos, scale)
+    return out
+
+
 def prefill_attention(q, k_cache, v_cache, block_tables, cu_seqlens_q, cu_seqlens_k, scale: float) -> torch.Tensor:
     q = torch.as_tensor(q).float()
     k_cache = torch.as_tensor(k_cache).float()

@@ -77,9 +77,10 @@ def _unit_tiles(u):
     return out
 
 
-def _coverage(cu_q, cu_k, H, Hk, num_sms):
+def _coverage(cu_q, cu_k, H, Hk, num_sms, causal=True, head_dim=128):
     from vlcache_b200 import ops
-    plan = ops.build_prefill_plan(cu_q, cu_k, H, Hk, num_sms=num_sms)
+    plan = ops.build_prefill_plan(cu_q, cu_k, H, Hk, head_dim, num_sms=num_sms, causal=causal)
+    assert int(plan.host[18]) == int(causal) and int(plan.host[19]) == head_dim
     grid, cta, units, merges, nparts = _decode_plan(plan)
     G = H // Hk
     T = 128 // G
@@ -92,7 +93,7 @@ def _coverage(cu_q, cu_k, H, Hk, num_sms):
         ql, kl = cu_q[b + 1] - cu_q[b], cu_k[b + 1] - cu_k[b]
         for g in range(Hk):
             for t in range(ql):
-                pos = kl - ql + t
+                pos = kl - ql + t if causal else kl - 1
                 for kb in range(pos // 128 + 1):
                     need[(cu_q[b] + t, g, kb)] = 0
     parts_seen = set()
@@ -137,6 +138,31 @@ def test_planner_covers_causal_pairs_exactly_once(H, Hk):
     cu_q = [0, 118, 150, 150 + 300, 150 + 300 + 9]
     cu_k = [0, 118, 118 + 1072, 118 + 1072 + 300, 118 + 1072 + 300 + 509]
     _coverage(cu_q, cu_k, H, Hk, num_sms=16)
+
+
+@pytest.mark.parametrize("H,Hk,d", [(16, 16, 80), (16, 2, 128), (28, 4, 96)])
+def test_planner_covers_noncausal_pairs_exactly_once(H, Hk, d):
+    """Non-causal plans (vision windows and full attention): every key block of a
+    sequence, for every query row of it, exactly once; ragged windows included."""
+    lens = [64, 64, 37, 64, 300, 1, 64, 129]
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    plan = _coverage(cu, cu, H, Hk, num_sms=16, causal=False, head_dim=d)
+    units = _decode_plan(plan)[2]
+    for u in units:
+        for (_, _, kp0, _, _, _) in _unit_tiles(u):
+            assert kp0 == int(u[4]) - 1          # non-causal rows see the whole sequence
+
+
+def test_planner_head_dims():
+    from vlcache_b200 import ops
+    from vlcache_b200._lib import VLCError
+    for d in (80, 96, 112, 128):
+        ops.build_prefill_plan([0, 64], [0, 64], 16, 16, d, causal=False)
+    for d in (64, 72, 136):
+        with pytest.raises((ValueError, VLCError)):
+            ops.build_prefill_plan([0, 64], [0, 64], 16, 16, d, causal=False)
 
 
 def test_planner_cfg2_balanced():

@@ -43,7 +43,7 @@ int validate(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_hea
              int head_dim) {
   if (!cu_q || !cu_k) return VLC_ERR_NULL;
   if (num_seqs < 0) return VLC_ERR_SHAPE;
-  if (head_dim != 128) return VLC_ERR_UNSUPPORTED;
+  if (head_dim <= 64 || head_dim > 128 || head_dim % 16 != 0) return VLC_ERR_UNSUPPORTED;
   if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return VLC_ERR_SHAPE;
   if (num_heads / num_kv_heads > kTileRows) return VLC_ERR_UNSUPPORTED;
   if (cu_q[0] != 0 || cu_k[0] != 0) return VLC_ERR_METADATA;
@@ -55,7 +55,10 @@ int validate(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_hea
   return VLC_OK;
 }
 
-void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_kv_heads, int T,
+// Causal: row t0 + r of a sequence sees keys <= k_len - q_len + t0 + r (flash-attn's
+// bottom-right alignment).  Non-causal: every row sees all k_len keys (kpos0 = k_len - 1,
+// the kernel adds no per-row offset).
+void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_kv_heads, int T, bool causal,
                  std::vector<Tile>& tiles) {
   size_t count = 0;
   for (int b = 0; b < num_seqs; ++b) count += (size_t)((cu_q[b + 1] - cu_q[b] + T - 1) / T) * num_kv_heads;
@@ -70,8 +73,8 @@ void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num
         t.kv_head = g;
         t.q_begin = cu_q[b] + t0;
         t.q_count = std::min(T, ql - t0);
-        t.kpos0 = kl - ql + t0;
-        const int max_pos = t.kpos0 + t.q_count - 1;
+        t.kpos0 = causal ? kl - ql + t0 : kl - 1;
+        const int max_pos = causal ? t.kpos0 + t.q_count - 1 : kl - 1;
         t.n_kb = max_pos / kBlockN + 1;
         t.kv_len = kl;
         t.k_base = cu_k[b];
@@ -83,14 +86,14 @@ void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num
 
 }  // namespace
 
-extern "C" int64_t vlc_prefill_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
-                                             int num_heads, int num_kv_heads, int num_sms) {
+extern "C" int64_t vlc_attention_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
+                                               int num_heads, int num_kv_heads, int causal, int num_sms) {
   if (validate(cu_q, cu_k, num_seqs, num_heads, num_kv_heads, 128) != VLC_OK) return -1;
   if (num_sms <= 0) num_sms = 148;
   const int G = num_heads / num_kv_heads;
   const int T = kTileRows / G;
   std::vector<Tile> tiles;
-  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, tiles);
+  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
   int64_t total_kb = 0;
   for (const Tile& t : tiles) total_kb += t.n_kb;
   const int64_t max_units = (int64_t)tiles.size() + total_kb;
@@ -98,9 +101,14 @@ extern "C" int64_t vlc_prefill_plan_capacity(const int32_t* cu_q, const int32_t*
          (int64_t)tiles.size() * (vlc::kMergeInts + kTileRows);
 }
 
-extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_heads,
-                                int num_kv_heads, int head_dim, int num_sms, int32_t* plan_out,
-                                int64_t plan_capacity, int64_t* plan_len) {
+extern "C" int64_t vlc_prefill_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
+                                             int num_heads, int num_kv_heads, int num_sms) {
+  return vlc_attention_plan_capacity(cu_q, cu_k, num_seqs, num_heads, num_kv_heads, 1, num_sms);
+}
+
+extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_heads,
+                                  int num_kv_heads, int head_dim, int causal, int num_sms, int32_t* plan_out,
+                                  int64_t plan_capacity, int64_t* plan_len) {
   using namespace vlc;
   const int v = validate(cu_q, cu_k, num_seqs, num_heads, num_kv_heads, head_dim);
   if (v != VLC_OK) return v;
@@ -109,7 +117,7 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   const int G = num_heads / num_kv_heads;
   const int T = kTileRows / G;
   std::vector<Tile> tiles;
-  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, tiles);
+  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
 
   // Pair the tiles of each (sequence, KV head) from the end: (last, second last),
   // ...; with an odd count the first (cheapest) tile stays alone.  The later tile
@@ -362,6 +370,8 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   h[kPTotalLen] = (int32_t)total;
   h[kPMergeBlocks] = (int32_t)merge_blocks.size();
   h[kPOffMergeBlocks] = (int32_t)off_mblocks;
+  h[kPCausal] = causal != 0 ? 1 : 0;
+  h[kPHeadDim] = head_dim;
   int32_t* cta = h + off_cta;
   int32_t* up = h + off_units;
   for (int c = 0; c <= grid; ++c) cta[c] = cta_begin[c];
@@ -375,4 +385,11 @@ extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int nu
   for (size_t i = 0; i < merge_blocks.size(); ++i) h[off_mblocks + i] = merge_blocks[i];
   *plan_len = total;
   return VLC_OK;
+}
+
+extern "C" int vlc_prefill_plan(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num_heads,
+                                int num_kv_heads, int head_dim, int num_sms, int32_t* plan_out,
+                                int64_t plan_capacity, int64_t* plan_len) {
+  return vlc_attention_plan(cu_q, cu_k, num_seqs, num_heads, num_kv_heads, head_dim, 1, num_sms, plan_out,
+                            plan_capacity, plan_len);
 }

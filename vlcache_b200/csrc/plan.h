@@ -8,7 +8,7 @@
 namespace vlc {
 
 constexpr int32_t kPlanMagic = 0x564C4350;  // 'VLCP'
-constexpr int32_t kPlanVersion = 4;
+constexpr int32_t kPlanVersion = 5;
 constexpr int kPlanHeaderInts = 20;
 
 // header fields
@@ -31,6 +31,8 @@ enum : int {
   kPTotalLen = 15,
   kPMergeBlocks = 16,     // blocks of the merge launch
   kPOffMergeBlocks = 17,  // int32[merge_blocks]: (merge index << 8) | first row of the block
+  kPCausal = 18,          // 1: row i of a sequence sees keys <= k_len - q_len + i; 0: all k_len keys
+  kPHeadDim = 19,         // head_dim the plan was made for (64 < d <= 128, d % 16 == 0)
 };
 
 // A unit is one or two query tiles of one (sequence, KV head) over one range of

@@ -79,8 +79,8 @@ constexpr uint32_t IDESC_PV = umma_idesc_bf16(128, 128, false, true);
 constexpr int kTileThreads = 128;  // softmax threads per tile
 
 struct Params {
-  CUtensorMap tm_q;   // dims {HD, num_heads, total_q}, box {64, G, T}
-  CUtensorMap tm_k;   // dims {HD, Hk, num_rows},    box {64, 1, BN}
+  CUtensorMap tm_q;   // dims {d, num_heads, total_q}, box {64, G, T} (columns >= d fill with 0)
+  CUtensorMap tm_k;   // dims {d, Hk, num_rows},    box {64, 1, BN}
   CUtensorMap tm_v;
   const int32_t* cta_offsets;  // [grid + 1]
   const int32_t* units;        // [num_units][kUnitInts]
@@ -91,13 +91,15 @@ struct Params {
   int rows;            // T * G (<= 128)
   float scale_log2;    // softmax_scale * log2(e)
   int64_t num_slots;
-  CUtensorMap tm_o;   // out:    dims {HD, num_heads, total_q}, box {64, G, T}
+  CUtensorMap tm_o;   // out:    dims {d, num_heads, total_q}, box {32, G, T}
   CUtensorMap tm_p;   // part_o: dims {HD, num_parts * BM},   box {64, BM}
   // Same tensors, 128-byte swizzle, box {64, G, T} / {64, BM}: the last epilogue of a
   // tile stores straight from the tile's Q slot (same layout as the Q load).
   CUtensorMap tm_o128;
   CUtensorMap tm_p128;
   int tokens_per_tile;  // T
+  int head_dim;         // d of q/k/v/out (64 < d <= 128); tiles are zero-padded to 128 columns
+  int causal;           // 0: every row sees all of its sequence's keys
   __nv_bfloat16* out;
   int64_t out_token_stride;
   int out_store32;        // out rows are 32-byte aligned: 256-bit stores
@@ -505,7 +507,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       const int part = u[x == 0 ? kUPartA : kUPartB];
       const int tok = row / p.group;
       const bool row_valid = row < p.rows && tok < q_count;
-      const int qpos = kpos0 + tok;
+      const int qpos = p.causal ? kpos0 + tok : kpos0;  // non-causal: kpos0 = k_len - 1
       float m_use = -INFINITY;
       float l_row = 0.f;
       bool ok = true;
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       __nv_bfloat16* dst;
       if (part < 0) {
         const int head = g * p.group + (row - tok * p.group);
-        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * HD;
+        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * p.head_dim;
       } else {
         // Split partial: O / l as bf16 (the merge re-weights by l and the max).
         dst = p.part_o + ((int64_t)part * BM + row) * HD;
@@ -649,10 +651,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         if (row == 0) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (part < 0)
-              tma_store_3d(&p.tm_o128, qs + h * HALF_BYTES, 64 * h, g * p.group, q_begin);
-            else
+            if (part < 0) {
+              if (64 * h < p.head_dim)  // columns past head_dim are the zero padding
+                tma_store_3d(&p.tm_o128, qs + h * HALF_BYTES, 64 * h, g * p.group, q_begin);
+            } else {
               tma_store_2d(&p.tm_p128, qs + h * HALF_BYTES, 64 * h, part * BM);
+            }
           }
           bulk_commit_group();
         }
@@ -674,10 +678,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           fence_proxy_async_smem();
           named_bar_sync(1 + x, kTileThreads);
           if (row == 0) {
-            if (part < 0)
-              tma_store_3d(&p.tm_o, buf, 32 * r, g * p.group, q_begin);
-            else
+            if (part < 0) {
+              if (32 * r < p.head_dim) tma_store_3d(&p.tm_o, buf, 32 * r, g * p.group, q_begin);
+            } else {
               tma_store_2d(&p.tm_p, buf, 32 * r, part * BM);
+            }
             bulk_commit_group();
           }
         }
@@ -686,11 +691,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         // the following tokens, so each valid row is written directly.
         if (p.out_store32) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) st_global_v8(dst + c * 16, *reinterpret_cast<const uint32_t(*)[8]>(&orr[c * 8]));
+          for (int c = 0; c < 8; ++c)
+            if (c * 16 < p.head_dim)
+              st_global_v8(dst + c * 16, *reinterpret_cast<const uint32_t(*)[8]>(&orr[c * 8]));
         } else {
 #pragma unroll
           for (int c = 0; c < 16; ++c)
-            *reinterpret_cast<uint4*>(dst + c * 8) = make_uint4(orr[4 * c], orr[4 * c + 1], orr[4 * c + 2], orr[4 * c + 3]);
+            if (c * 8 < p.head_dim)
+              *reinterpret_cast<uint4*>(dst + c * 8) =
+                  make_uint4(orr[4 * c], orr[4 * c + 1], orr[4 * c + 2], orr[4 * c + 3]);
         }
       }
       tc_fence_before();
@@ -719,7 +728,7 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
                                                                const __nv_bfloat16* __restrict__ part_o,
                                                                const float* __restrict__ part_ml, int group,
                                                                __nv_bfloat16* __restrict__ out,
-                                                               int64_t out_token_stride) {
+                                                               int64_t out_token_stride, int head_dim) {
   const int entry = __ldg(blocks + blockIdx.x);
   const int32_t* m = merges + (int64_t)(entry >> 8) * kMergeInts;
   const int q_begin = __ldg(m + kMQBegin), g = __ldg(m + kMKvHead);
@@ -797,11 +806,11 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
     }
     m_run = m_all;
   }
-  if (!active || k0 != 0) return;
+  if (!active || k0 != 0 || c * 16 >= head_dim) return;  // dims past head_dim: zero padding
   const float inv = L > 0.f ? 1.0f / L : 0.f;
   const int tok = row / group;
   const int head = g * group + (row - tok * group);
-  __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * HD + c * 16;
+  __nv_bfloat16* dst = out + (int64_t)(q_begin + tok) * out_token_stride + (int64_t)head * head_dim + c * 16;
   uint4 p0, p1;
   p0.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
   p0.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
@@ -835,20 +844,21 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
                                 void* out, int64_t out_token_stride, void* workspace,
                                 int64_t workspace_bytes, void* stream) {
   if (!q || !k_cache || !v_cache || !plan_dev || !plan_host || !out) return VLC_ERR_NULL;
-  if (head_dim != HD) return VLC_ERR_UNSUPPORTED;
+  if (head_dim <= 64 || head_dim > HD || head_dim % 16 != 0) return VLC_ERR_UNSUPPORTED;
   if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return VLC_ERR_SHAPE;
   if (block_tables && (block_size <= 0 || block_size % BN != 0)) return VLC_ERR_UNSUPPORTED;
   if (plan_host[kPMagic] != kPlanMagic || plan_host[kPVersion] != kPlanVersion) return VLC_ERR_PLAN;
   const int group = num_heads / num_kv_heads;
   if (plan_host[kPGroup] != group || plan_host[kPNumHeads] != num_heads ||
-      plan_host[kPNumKvHeads] != num_kv_heads || plan_host[kPTotalQ] != total_q)
+      plan_host[kPNumKvHeads] != num_kv_heads || plan_host[kPTotalQ] != total_q ||
+      plan_host[kPHeadDim] != head_dim)
     return VLC_ERR_PLAN;
   const int grid = plan_host[kPGrid];
   if (grid == 0 || total_q == 0) return VLC_OK;
   if (q_token_stride % 8 != 0 || out_token_stride % 8 != 0 || k_row_stride % 8 != 0 || v_row_stride % 8 != 0)
     return VLC_ERR_STRIDE;
-  if (q_token_stride < (int64_t)num_heads * HD || out_token_stride < (int64_t)num_heads * HD ||
-      k_row_stride < (int64_t)num_kv_heads * HD || v_row_stride < (int64_t)num_kv_heads * HD)
+  if (q_token_stride < (int64_t)num_heads * head_dim || out_token_stride < (int64_t)num_heads * head_dim ||
+      k_row_stride < (int64_t)num_kv_heads * head_dim || v_row_stride < (int64_t)num_kv_heads * head_dim)
     return VLC_ERR_STRIDE;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) return VLC_ERR_ALIGN;
   const int64_t ws_need = vlc_prefill_workspace_size(plan_host);
@@ -859,22 +869,22 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   const int T = plan_host[kPTokensPerTile];
   const int rows = plan_host[kPRowsPerTile];
   {
-    const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_heads, (uint64_t)total_q};
-    const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)q_token_stride * 2};
+    const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_heads, (uint64_t)total_q};
+    const uint64_t strides[2] = {(uint64_t)head_dim * 2, (uint64_t)q_token_stride * 2};
     const uint32_t box[3] = {64, (uint32_t)group, (uint32_t)T};
     if (encode_tmap_bf16(&prm.tm_q, q, 3, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_kv_heads, (uint64_t)num_slots};
-    const uint64_t ks[2] = {(uint64_t)HD * 2, (uint64_t)k_row_stride * 2};
-    const uint64_t vs[2] = {(uint64_t)HD * 2, (uint64_t)v_row_stride * 2};
+    const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_kv_heads, (uint64_t)num_slots};
+    const uint64_t ks[2] = {(uint64_t)head_dim * 2, (uint64_t)k_row_stride * 2};
+    const uint64_t vs[2] = {(uint64_t)head_dim * 2, (uint64_t)v_row_stride * 2};
     const uint32_t box[3] = {64, 1, (uint32_t)BN};
     if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, ks, box, 128) != VLC_OK) return VLC_ERR_CUDA;
     if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, vs, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)num_heads, (uint64_t)total_q};
-    const uint64_t strides[2] = {(uint64_t)HD * 2, (uint64_t)out_token_stride * 2};
+    const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_heads, (uint64_t)total_q};
+    const uint64_t strides[2] = {(uint64_t)head_dim * 2, (uint64_t)out_token_stride * 2};
     const uint32_t box[3] = {32, (uint32_t)group, (uint32_t)T};
     if (encode_tmap_bf16(&prm.tm_o, out, 3, dims, strides, box, 64) != VLC_OK) return VLC_ERR_CUDA;
     const uint32_t box128[3] = {64, (uint32_t)group, (uint32_t)T};
@@ -908,6 +918,8 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     prm.tm_p128 = prm.tm_o128;
   }
   prm.tokens_per_tile = T;
+  prm.head_dim = head_dim;
+  prm.causal = plan_host[kPCausal];
 
   static std::atomic<uint64_t> smem_set{0};
   if (ensure_dynamic_smem((const void*)prefill_attn_kernel, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
@@ -941,7 +953,7 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     mcfg.numAttrs = 1;
     if (cudaLaunchKernelEx(&mcfg, prefill_merge_kernel, (const int32_t*)(plan_dev + plan_host[kPOffMerges]),
                            (const int32_t*)(plan_dev + plan_host[kPOffMergeBlocks]), (const __nv_bfloat16*)prm.part_o,
-                           (const float*)prm.part_ml, group, prm.out, out_token_stride) != cudaSuccess) {
+                           (const float*)prm.part_ml, group, prm.out, out_token_stride, head_dim) != cudaSuccess) {
       (void)cudaGetLastError();
       rc = VLC_ERR_CUDA;
     }

@@ -206,22 +206,25 @@ class PrefillPlan:
 
 
 def build_prefill_plan(cu_seqlens_q, cu_seqlens_k, num_heads: int, num_kv_heads: int, head_dim: int = HEAD_DIM,
-                       num_sms: int = 0, device: torch.device | str | None = None) -> PrefillPlan:
-    """Plan the warm-prefill attention launch from HOST cu_seqlens (lists/arrays/CPU tensors)."""
+                       num_sms: int = 0, device: torch.device | str | None = None, causal: bool = True) -> PrefillPlan:
+    """Plan the warm-prefill attention launch from HOST cu_seqlens (lists/arrays/CPU tensors).
+    ``causal=False`` plans the non-causal varlen attention (every row sees all keys of its
+    sequence); ``head_dim`` may be 80..128 in steps of 16."""
     cq = np.ascontiguousarray(np.asarray(cu_seqlens_q, dtype=np.int32))
     ck = np.ascontiguousarray(np.asarray(cu_seqlens_k, dtype=np.int32))
     nseq = len(cq) - 1
     assert len(ck) == nseq + 1
     L = lib()
     sms = int(num_sms) if num_sms else (L.vlc_num_sms() if device is not None else 148)
-    cap = L.vlc_prefill_plan_capacity(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads, sms)
+    cap = L.vlc_attention_plan_capacity(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads,
+                                        1 if causal else 0, sms)
     if cap < 0:
         raise ValueError("invalid prefill metadata (cu_seqlens / heads)")
     plan = np.zeros(int(cap), dtype=np.int32)
     used = ctypes.c_int64(0)
-    st = L.vlc_prefill_plan(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads, head_dim, sms,
-                            plan.ctypes.data, int(cap), ctypes.byref(used))
-    check("vlc_prefill_plan", st)
+    st = L.vlc_attention_plan(cq.ctypes.data, ck.ctypes.data, nseq, num_heads, num_kv_heads, head_dim,
+                              1 if causal else 0, sms, plan.ctypes.data, int(cap), ctypes.byref(used))
+    check("vlc_attention_plan", st)
     plan = plan[: used.value].copy()
     ws = int(L.vlc_prefill_workspace_size(plan.ctypes.data))
     dev = None
