@@ -734,6 +734,9 @@ __global__ void __launch_bounds__(256, 3) prefill_merge_kernel(const int32_t* __
   const int q_begin = __ldg(m + kMQBegin), g = __ldg(m + kMKvHead);
   const int part0 = __ldg(m + kMPartBegin), nparts = __ldg(m + kMNumParts);
   const int R = __ldg(m + kMRowsPerWarp), nrows = __ldg(m + kMRows);
+  // The next kernel may be scheduled now: every programmatic dependent here waits
+  // (griddepcontrol.wait) for this grid to complete before it reads the output.
+  pdl_launch_dependents();
   pdl_wait();  // the partials are written by the attention kernel launched just before
   const int K = 4 / R;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
