@@ -924,7 +924,39 @@ def cpu_reference_sample(budget_s: float = 12.0):
 def run_only(args, device):
     """One kernel family in isolation, eager launches (used for the ncu captures)."""
     res = {"only": args.only}
-    if args.only == "vision":
+    if args.only == "kernels":
+        # One eager launch of each newer kernel per round (3 rounds), sized for an ncu capture
+        # (a few hundred MB on the device): gate_up+SiLU and qkv+RoPE+scatter GEMMs on cfg2's
+        # 1,123 rows (3B), the content hash of a 4K image, a full-attention vision block over a
+        # 1080p image (10,764 patches, 16 heads x 80, non-causal).
+        from vlcache_b200 import ops
+        from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+        from vlcache_b200.layers.vision_attention import plan_varlen
+        g = torch.Generator(device=device).manual_seed(1)
+        m, hid, inter = 1123, 2048, 11008
+        x = torch.randn(m, hid, generator=g, device=device).to(torch.bfloat16)
+        wgu = (torch.randn(2 * inter, hid, generator=g, device=device) / 45.0).to(torch.bfloat16)
+        wqkv = (torch.randn(20 * D, hid, generator=g, device=device) / 45.0).to(torch.bfloat16)
+        bqkv = torch.randn(20 * D, generator=g, device=device).to(torch.bfloat16)
+        table = rope_cos_sin_cache(D, 32768, 1e6).to(device)
+        pos = torch.randint(0, 32768, (m,), generator=g, device=device)
+        kc = torch.zeros(8, BLOCK, HK, D, dtype=torch.bfloat16, device=device)
+        vc = torch.zeros_like(kc)
+        slots = torch.randperm(8 * BLOCK, generator=g, device=device)[:m].to(torch.int32)
+        px = torch.randn(42196, 1176, generator=g, device=device)
+        n_v = 39 * 69 * 4
+        qv = torch.randn(n_v, 16, 80, generator=g, device=device).to(torch.bfloat16)
+        cu = np.array([0, n_v], np.int32)
+        vplan = plan_varlen(cu, cu, 16, 16, 80, causal=False, device=device)
+        t0 = time.perf_counter()
+        for _ in range(3):
+            ops.linear_silu_mul(x, wgu)
+            ops.qkv_rope_store_kvcache(x, wqkv, bqkv, pos, table, kc, vc, slots, H, HK)
+            ops.content_hash_device_async(px, b"grid")
+            ops.prefill_attention(qv, qv, qv, None, vplan, 80 ** -0.5)
+        torch.cuda.synchronize()
+        res["wall_ms"] = (time.perf_counter() - t0) * 1e3
+    elif args.only == "vision":
         res["vision_attention"] = vision_attention_bench(device, peaks()[1], reps=max(1, args.steps))
     elif args.only == "hash":
         res["encoder_hash"] = encoder_hash_bench(device, peaks()[0], reps=max(1, args.steps))
@@ -1025,7 +1057,7 @@ def main():
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip timing flash-attn (the reference's kernels) on the same inputs")
     ap.add_argument("--only", choices=["prefill", "prefill_7b_full", "decode", "shift", "scatter", "cfg3", "rope",
-                                       "linear", "hash", "vision"],
+                                       "linear", "hash", "vision", "kernels"],
                     help="run just one kernel's loop (eager launches, for ncu captures) and print its timing")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
