@@ -20,6 +20,15 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=[1, 2], ids=["single_sm", "cta_pair"])
+def kernel_mode(request, cuda_lib):
+    """Run a test on the single-SM GEMM and on the CTA-pair (cta_group::2) GEMM."""
+    from vlcache_b200 import ops
+    ops.set_linear_kernel(request.param)
+    yield request.param
+    ops.set_linear_kernel(0)
+
+
 def _ref_linear(x, w, b=None):
     y = x.float() @ w.float().t()
     if b is not None:
@@ -55,7 +64,7 @@ def _assert_close_ulp(out, ref, what, margins, bound=ONE_ULP):
     (129, 136, 64, True),         # N tail inside a 32-column chunk, M tail
     (300, 520, 200, False),       # K not a multiple of 64
 ])
-def test_linear_matches_fp32(cuda_lib, margins, m, n, k, bias):
+def test_linear_matches_fp32(kernel_mode, margins, m, n, k, bias):
     from vlcache_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(m + n + k)
     x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
@@ -73,6 +82,7 @@ def test_linear_stream_k(cuda_lib, margins, m, n, k):
     the CTA that completes them) against fp32, against whole-tile launches, run to run
     bit-identical, and the workspace's tickets left at zero for the next launch."""
     from vlcache_b200 import ops
+    ops.set_linear_kernel(1)   # stream-K belongs to the single-SM kernel
     g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
     x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
     w = (torch.randn(n, k, generator=g, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
@@ -90,9 +100,10 @@ def test_linear_stream_k(cuda_lib, margins, m, n, k):
     tiles = -(-m // 128) * -(-n // 256)
     off = 2 * ops.num_sms() * 128 * 256 * 4   # the tickets follow the per-SM partial slots
     assert int(ws[off:off + 4 * tiles].view(torch.int32).abs().sum()) == 0
+    ops.set_linear_kernel(0)
 
 
-def test_linear_strided_input_and_output(cuda_lib, margins):
+def test_linear_strided_input_and_output(kernel_mode, margins):
     """x and out as column slices of wider buffers (row strides != widths)."""
     from vlcache_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -108,7 +119,7 @@ def test_linear_strided_input_and_output(cuda_lib, margins):
 
 
 @pytest.mark.parametrize("m,inter,k", [(1123, 11008, 2048), (1123, 18944, 3584), (77, 200, 128)])
-def test_linear_silu_mul(cuda_lib, margins, m, inter, k):
+def test_linear_silu_mul(kernel_mode, margins, m, inter, k):
     from vlcache_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(m + inter)
     x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
@@ -123,7 +134,7 @@ def test_linear_silu_mul(cuda_lib, margins, m, inter, k):
 
 
 @pytest.mark.parametrize("H,Hk,hidden", [(16, 2, 2048), (28, 4, 3584)])
-def test_qkv_rope_store_bit_exact_vs_unfused(cuda_lib, margins, H, Hk, hidden):
+def test_qkv_rope_store_bit_exact_vs_unfused(kernel_mode, margins, H, Hk, hidden):
     from oracle import rope as orope
     from vlcache_b200 import ops
     from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache

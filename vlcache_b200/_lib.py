@@ -51,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_content_hash_host": (c_int, [c_vp, c_i64, c_vp, c_int, c_int, c_vp]),
     "vlc_xxh64": (ctypes.c_uint64, [c_vp, c_i64, ctypes.c_uint64]),
     "vlc_linear_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),
+    "vlc_linear_set_kernel": (c_int, [c_int]),
     "vlc_linear": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
     "vlc_linear_silu_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_int, c_vp, c_i64,
                                     c_vp]),

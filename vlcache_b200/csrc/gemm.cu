@@ -232,6 +232,142 @@ __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, cons
   }
 }
 
+// The epilogue of one accumulator tile: thread = row r_in of the tile (global row `row`),
+// output columns of tile nt.  Values come from this CTA's TMEM (`tacc`), plus the other
+// CTAs' partials in a stream-K fix-up (fx).
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, const Fixup& fx, int r_in, int row,
+                                              int nt) {
+  const bool row_ok = row < p.m;
+  if (EPI == kPlain) {
+    const int n0 = nt * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      load_acc32(p, tacc + c * 32, fx, r_in, c * 32, v);
+      const int col = n0 + c * 32;
+      if (!row_ok || col >= p.n) continue;
+      float b[32];
+      load_bias32(p.bias, col, p.n, b);
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = pack2(v[2 * i] + b[2 * i], v[2 * i + 1] + b[2 * i + 1]);
+      __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
+      if (col + 32 <= p.n) {
+        store32(dst, w);
+      } else {
+        for (int g = 0; g < 4; ++g)
+          if (col + 8 * g < p.n)
+            reinterpret_cast<uint4*>(dst)[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+      }
+    }
+  } else if (EPI == kSiluMul) {
+    // TMEM columns [0, 128): gate of output columns n0 + [0, 128); [128, 256): up.
+    const int n0 = nt * (BN / 2);
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      float g[32], u[32];
+      load_acc32(p, tacc + c * 32, fx, r_in, c * 32, g);
+      load_acc32(p, tacc + BN / 2 + c * 32, fx, r_in, BN / 2 + c * 32, u);
+      const int col = n0 + c * 32;
+      if (!row_ok || col >= p.n) continue;
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float o[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          // gate_up_proj's output is bf16; SiluAndMul evaluates silu(x) * y in fp32
+          const float x = bf16_round(g[2 * i + e]);
+          const float y = bf16_round(u[2 * i + e]);
+          o[e] = x / (1.0f + __expf(-x)) * y;
+        }
+        w[i] = pack2(o[0], o[1]);
+      }
+      __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
+      if (col + 32 <= p.n) {
+        store32(dst, w);
+      } else {
+        for (int q = 0; q < 4; ++q)
+          if (col + 8 * q < p.n)
+            reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      }
+    }
+  } else {
+    // kQkvRope: the tile's 256 columns are two heads of the [q | k | v] layout.
+    int64_t pos = 0, slot = -1;
+    bool pos_ok = false, slot_ok = false;
+    if (row_ok) {
+      pos = __ldg(p.positions + row);
+      slot = __ldg(p.slot_mapping + row);
+      pos_ok = pos >= 0 && pos < p.max_position;
+      slot_ok = slot >= -1 && slot < p.num_slots;
+    }
+#pragma unroll 1
+    for (int hh = 0; hh < 2; ++hh) {
+      const int head = nt * 2 + hh;
+      const bool is_q = head < p.num_heads;
+      const bool is_v = head >= p.num_heads + p.num_kv_heads;
+      const int col0 = head * HD;
+      // the head's 128 columns in two rounds of (x1: 32 of the first half, x2: the
+      // matching 32 of the second half)
+#pragma unroll 1
+      for (int r = 0; r < 2; ++r) {
+        float x1[32], x2[32];
+        load_acc32(p, tacc + hh * HD + r * 32, fx, r_in, hh * HD + r * 32, x1);
+        load_acc32(p, tacc + hh * HD + 64 + r * 32, fx, r_in, hh * HD + 64 + r * 32, x2);
+        if (!row_ok || col0 >= p.n) continue;
+        if (!slot_ok || (!is_v && !pos_ok)) {
+          if (hh == 0 && r == 0) record_error(!slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
+          continue;
+        }
+        __nv_bfloat16* dst;
+        if (is_q) {
+          dst = p.q_out + (int64_t)row * p.q_out_stride + (int64_t)head * HD;
+        } else {
+          if (slot < 0) continue;
+          const int kvh = is_v ? head - p.num_heads - p.num_kv_heads : head - p.num_heads;
+          dst = (is_v ? p.v_cache : p.k_cache) + slot * ((int64_t)p.num_kv_heads * HD) + (int64_t)kvh * HD;
+        }
+        float bx[32], by[32];
+        load_bias32(p.bias, col0 + r * 32, p.n, bx);
+        load_bias32(p.bias, col0 + 64 + r * 32, p.n, by);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x1[i] = bf16_round(x1[i] + bx[i]);  // the linear's bf16 output
+          x2[i] = bf16_round(x2[i] + by[i]);
+        }
+        if (!is_v) {
+          // apply_rotary_emb in fp32, each product and sum rounded on its own
+          const float* cs = p.cos_sin + pos * HD;
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + r * 32) + i4);
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + 64 + r * 32) + i4);
+            const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * i4 + e;
+              const float y1 = __fsub_rn(__fmul_rn(x1[i], cv[e]), __fmul_rn(x2[i], sv[e]));
+              const float y2 = __fadd_rn(__fmul_rn(x2[i], cv[e]), __fmul_rn(x1[i], sv[e]));
+              x1[i] = y1;
+              x2[i] = y2;
+            }
+          }
+        }
+        uint32_t w1[16], w2[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          w1[i] = pack2(x1[2 * i], x1[2 * i + 1]);
+          w2[i] = pack2(x2[2 * i], x2[2 * i + 1]);
+        }
+        store32(dst + r * 32, w1);
+        store32(dst + 64 + r * 32, w2);
+      }
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -353,7 +489,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
       const int row = mt * BM + r_in;
-      const bool row_ok = row < p.m;
       Fixup fx;
       fx.t = t;
       fx.c_lo = 1;
@@ -397,133 +532,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
         fx.c_lo = c_lo;
         fx.c_hi = c_hi;
       }
-      if (EPI == kPlain) {
-        const int n0 = nt * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          load_acc32(p, tacc + c * 32, fx, r_in, c * 32, v);
-          const int col = n0 + c * 32;
-          if (!row_ok || col >= p.n) continue;
-          float b[32];
-          load_bias32(p.bias, col, p.n, b);
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = pack2(v[2 * i] + b[2 * i], v[2 * i + 1] + b[2 * i + 1]);
-          __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
-          if (col + 32 <= p.n) {
-            store32(dst, w);
-          } else {
-            for (int g = 0; g < 4; ++g)
-              if (col + 8 * g < p.n)
-                reinterpret_cast<uint4*>(dst)[g] = make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
-          }
-        }
-      } else if (EPI == kSiluMul) {
-        // TMEM columns [0, 128): gate of output columns n0 + [0, 128); [128, 256): up.
-        const int n0 = nt * (BN / 2);
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          float g[32], u[32];
-          load_acc32(p, tacc + c * 32, fx, r_in, c * 32, g);
-          load_acc32(p, tacc + BN / 2 + c * 32, fx, r_in, BN / 2 + c * 32, u);
-          const int col = n0 + c * 32;
-          if (!row_ok || col >= p.n) continue;
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float o[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              // gate_up_proj's output is bf16; SiluAndMul evaluates silu(x) * y in fp32
-              const float x = bf16_round(g[2 * i + e]);
-              const float y = bf16_round(u[2 * i + e]);
-              o[e] = x / (1.0f + __expf(-x)) * y;
-            }
-            w[i] = pack2(o[0], o[1]);
-          }
-          __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
-          if (col + 32 <= p.n) {
-            store32(dst, w);
-          } else {
-            for (int q = 0; q < 4; ++q)
-              if (col + 8 * q < p.n)
-                reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-          }
-        }
-      } else {
-        // kQkvRope: the tile's 256 columns are two heads of the [q | k | v] layout.
-        int64_t pos = 0, slot = -1;
-        bool pos_ok = false, slot_ok = false;
-        if (row_ok) {
-          pos = __ldg(p.positions + row);
-          slot = __ldg(p.slot_mapping + row);
-          pos_ok = pos >= 0 && pos < p.max_position;
-          slot_ok = slot >= -1 && slot < p.num_slots;
-        }
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const int head = nt * 2 + hh;
-          const bool is_q = head < p.num_heads;
-          const bool is_v = head >= p.num_heads + p.num_kv_heads;
-          const int col0 = head * HD;
-          // the head's 128 columns in two rounds of (x1: 32 of the first half, x2: the
-          // matching 32 of the second half)
-#pragma unroll 1
-          for (int r = 0; r < 2; ++r) {
-            float x1[32], x2[32];
-            load_acc32(p, tacc + hh * HD + r * 32, fx, r_in, hh * HD + r * 32, x1);
-            load_acc32(p, tacc + hh * HD + 64 + r * 32, fx, r_in, hh * HD + 64 + r * 32, x2);
-            if (!row_ok || col0 >= p.n) continue;
-            if (!slot_ok || (!is_v && !pos_ok)) {
-              if (hh == 0 && r == 0) record_error(!slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
-              continue;
-            }
-            __nv_bfloat16* dst;
-            if (is_q) {
-              dst = p.q_out + (int64_t)row * p.q_out_stride + (int64_t)head * HD;
-            } else {
-              if (slot < 0) continue;
-              const int kvh = is_v ? head - p.num_heads - p.num_kv_heads : head - p.num_heads;
-              dst = (is_v ? p.v_cache : p.k_cache) + slot * ((int64_t)p.num_kv_heads * HD) + (int64_t)kvh * HD;
-            }
-            float bx[32], by[32];
-            load_bias32(p.bias, col0 + r * 32, p.n, bx);
-            load_bias32(p.bias, col0 + 64 + r * 32, p.n, by);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              x1[i] = bf16_round(x1[i] + bx[i]);  // the linear's bf16 output
-              x2[i] = bf16_round(x2[i] + by[i]);
-            }
-            if (!is_v) {
-              // apply_rotary_emb in fp32, each product and sum rounded on its own
-              const float* cs = p.cos_sin + pos * HD;
-#pragma unroll
-              for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + r * 32) + i4);
-                const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + 64 + r * 32) + i4);
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int i = 4 * i4 + e;
-                  const float y1 = __fsub_rn(__fmul_rn(x1[i], cv[e]), __fmul_rn(x2[i], sv[e]));
-                  const float y2 = __fadd_rn(__fmul_rn(x2[i], cv[e]), __fmul_rn(x1[i], sv[e]));
-                  x1[i] = y1;
-                  x2[i] = y2;
-                }
-              }
-            }
-            uint32_t w1[16], w2[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w1[i] = pack2(x1[2 * i], x1[2 * i + 1]);
-              w2[i] = pack2(x2[2 * i], x2[2 * i + 1]);
-            }
-            store32(dst + r * 32, w1);
-            store32(dst + 64 + r * 32, w2);
-          }
-        }
-      }
+      epilogue_tile<EPI>(p, tacc, fx, r_in, row, nt);
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
       if (*abort_flag) break;
@@ -534,6 +543,169 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// The same GEMM on CTA pairs (clusters of 2, tcgen05.mma.cta_group::2): an output tile is
+// 256 x 256; CTA rank r of the pair holds rows [128 r, 128 r + 128) of x's tile and rows
+// [128 r, 128 r + 128) of W's tile (kSiluMul: rank 0 the gate rows, rank 1 the up rows),
+// 32 KB a stage in a 6-stage ring.  Per 64-wide K block one SM reads 8 KB of operands per
+// 128 x 256 x 16 of MMA work, against 12 KB in the single-SM kernel.
+//   * both CTAs' TMA loads complete on the leader's (rank 0) full barrier, which the leader's
+//     producer arms for both CTAs' bytes;
+//   * the leader issues 4 MMAs of 256 x 256 x 16 per K block and commits to the stage's empty
+//     barrier, and after a tile's last block to acc_full, in both CTAs (multicast commit);
+//   * each CTA's epilogue reads its own 128 accumulator rows and arrives on the leader's
+//     acc_empty (256 arrivals) so the leader can reuse the TMEM half;
+//   * a cluster barrier after set-up (barriers initialised, TMEM allocated) and before
+//     exit (no remote arrival lands on a CTA that has left).
+// Whole tiles only: pair p takes tiles p, p + #pairs, ... (M-fastest).
+constexpr int PAIR_STAGES = 6;
+constexpr int PA_BYTES = 128 * BK * 2;            // 16 KB: this CTA's rows of x
+constexpr int PB_BYTES = 128 * BK * 2;            // 16 KB: this CTA's rows of W
+constexpr int PSTAGE = PA_BYTES + PB_BYTES;       // 32 KB
+constexpr int P_OFF_BAR = PAIR_STAGES * PSTAGE;
+constexpr int P_NUM_BARS = 2 * PAIR_STAGES + 4;
+constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
+constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t IDESC_PAIR = umma_idesc_bf16(2 * BM, BN, false, false);
+constexpr int PM = 2 * BM;  // output rows of a pair tile
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_OFF_BAR);
+  uint64_t* empty = full + PAIR_STAGES;
+  uint64_t* acc_full = full + 2 * PAIR_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P_OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + P_OFF_MISC + 4);
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 2 * 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_a);
+    tma_prefetch_desc(&p.tm_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before either uses the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      pdl_wait();  // x may be written by the kernel launched just before
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.tiles; t += npairs) {
+        const int mt = t % p.m_tiles, nt = t / p.m_tiles;
+        const int b_row = EPI == kSiluMul ? (rank == 0 ? nt * (BN / 2) : p.up_row0 + nt * (BN / 2))
+                                          : nt * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % PAIR_STAGES;
+          if (it >= PAIR_STAGES &&
+              !wait_bar(empty + s, (uint32_t)((it / PAIR_STAGES) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 44, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_expect_tx(full + s, 2 * PSTAGE);  // both CTAs' bytes
+          const uint32_t bar = mapa_shared(smem_u32(full + s), 0);
+          uint8_t* a_dst = smem + s * PSTAGE;
+          tma_load_2d_pair(a_dst, &p.tm_a, bar, kb * BK, mt * PM + (int)rank * BM);
+          tma_load_2d_pair(a_dst + PA_BYTES, &p.tm_b, bar, kb * BK, b_row);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      const uint32_t base_lo = umma_desc_sw128_lo(smem_u32(smem), 16);
+      constexpr uint32_t hi = umma_desc_sw128_hi(1024);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.tiles; t += npairs, ++local) {
+        const int buf = local & 1;
+        if (local >= 2 &&
+            !wait_bar(acc_empty + buf, (uint32_t)((local >> 1) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 45, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % PAIR_STAGES;
+          if (!wait_bar(full + s, (uint32_t)(it / PAIR_STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 46, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_lo = base_lo + (uint32_t)((s * PSTAGE) >> 4);
+          const uint32_t b_lo = a_lo + (uint32_t)(PA_BYTES >> 4);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_ss_pair(d, a_lo + (uint32_t)(k * 2), hi, b_lo + (uint32_t)(k * 2), hi, IDESC_PAIR,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(empty + s, 0x3);
+        }
+        if (!ok) break;
+        umma_commit_pair(acc_full + buf, 0x3);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2-5, both CTAs)
+    pdl_wait();
+    const int quarter = warp & 3;
+    const int r_in = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    Fixup fx;
+    fx.t = 0;
+    fx.c_lo = 1;
+    fx.c_hi = 0;
+    int local = 0;
+    for (int t = pair; t < p.tiles; t += npairs, ++local) {
+      const int mt = t % p.m_tiles, nt = t / p.m_tiles;
+      const int buf = local & 1;
+      if (!wait_bar(acc_full + buf, (uint32_t)(local >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 47, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
+      epilogue_tile<EPI>(p, tacc, fx, r_in, mt * PM + (int)rank * BM + r_in, nt);
+      tc_fence_before();
+      if (rank == 0)
+        mbar_arrive(acc_empty + buf);
+      else
+        mbar_arrive_cluster(mapa_shared(smem_u32(acc_empty + buf), 0));
+      if (*abort_flag) break;
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // every remote arrival and every MMA into this CTA's TMEM is done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -619,6 +791,79 @@ int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, 
   return VLC_OK;
 }
 
+// Kernel selection: 0 = automatic, 1 = single-SM tiles (stream-K where it pays), 2 = CTA pairs.
+static std::atomic<int> g_kernel_mode{0};
+
+template <int EPI>
+int launch_pair(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t w_rows, void* stream) {
+  {
+    const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)prm.m};
+    const uint64_t strides[1] = {(uint64_t)lda * 2};
+    const uint32_t box[2] = {BK, BM};
+    if (encode_tmap_bf16(&prm.tm_a, a, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)w_rows};
+    const uint64_t strides[1] = {(uint64_t)ldw * 2};
+    const uint32_t box[2] = {BK, (uint32_t)(BN / 2)};
+    if (encode_tmap_bf16(&prm.tm_b, w, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  }
+  prm.m_tiles = (prm.m + PM - 1) / PM;
+  prm.n_tiles = EPI == kSiluMul ? (prm.n + BN / 2 - 1) / (BN / 2) : (prm.n + BN - 1) / BN;
+  prm.tiles = prm.m_tiles * prm.n_tiles;
+  prm.k_blocks = (prm.k + BK - 1) / BK;
+  prm.total_kb = 0;
+  prm.partials = nullptr;
+  prm.counters = nullptr;
+  static std::atomic<uint64_t> smem_set{0};
+  if (ensure_dynamic_smem((const void*)gemm_pair_kernel<EPI>, P_SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  // Pairs resident at once (clusters of two SMs), queried once per device.
+  static std::atomic<int> max_pairs_dev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VLC_ERR_CUDA;
+  int max_pairs = max_pairs_dev[dev].load();
+  if (max_pairs <= 0) {
+    cfg.gridDim = dim3(2 * std::max(1, vlc_num_sms() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_pair_kernel<EPI>, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = std::max(1, vlc_num_sms() / 2);
+    }
+    max_pairs = n;
+    max_pairs_dev[dev].store(n);
+  }
+  cfg.gridDim = dim3(2 * std::min(prm.tiles, max_pairs));
+  if (cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, prm) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return VLC_ERR_CUDA;
+  }
+  return VLC_OK;
+}
+
+// Which kernel runs a launch: the pair kernel unless single-SM tiles are asked for or the
+// stream-K split applies (workspace given and tiles few and long).
+template <int EPI>
+int dispatch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t w_rows, void* workspace,
+             int64_t ws_bytes, void* stream) {
+  const int mode = g_kernel_mode.load();
+  if (mode == 2) return launch_pair<EPI>(prm, a, lda, w, ldw, w_rows, stream);
+  if (mode == 1) return launch<EPI>(prm, a, lda, w, ldw, w_rows, workspace, ws_bytes, stream);
+  return launch_pair<EPI>(prm, a, lda, w, ldw, w_rows, stream);
+}
+
 int check_common(const void* a, int64_t lda, const void* w, int64_t ldw, int m, int k) {
   if (!a || !w) return VLC_ERR_NULL;
   if (m < 0 || k <= 0) return VLC_ERR_SHAPE;
@@ -656,7 +901,7 @@ extern "C" int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_
   prm.out = (__nv_bfloat16*)out;
   prm.ldo = ldo;
   prm.bias = (const __nv_bfloat16*)bias;
-  return launch<kPlain>(prm, x, ldx, weight, ldw, n, workspace, workspace_bytes, stream);
+  return dispatch<kPlain>(prm, x, ldx, weight, ldw, n, workspace, workspace_bytes, stream);
 }
 
 extern "C" int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_up_weight, int64_t ldw, void* out,
@@ -676,7 +921,7 @@ extern "C" int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_
   prm.out = (__nv_bfloat16*)out;
   prm.ldo = ldo;
   prm.up_row0 = intermediate;
-  return launch<kSiluMul>(prm, x, ldx, gate_up_weight, ldw, 2LL * intermediate, workspace, workspace_bytes,
+  return dispatch<kSiluMul>(prm, x, ldx, gate_up_weight, ldw, 2LL * intermediate, workspace, workspace_bytes,
                           stream);
 }
 
@@ -715,5 +960,11 @@ extern "C" int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void
   prm.num_slots = num_slots;
   prm.num_heads = num_heads;
   prm.num_kv_heads = num_kv_heads;
-  return launch<kQkvRope>(prm, x, ldx, qkv_weight, ldw, n, workspace, workspace_bytes, stream);
+  return dispatch<kQkvRope>(prm, x, ldx, qkv_weight, ldw, n, workspace, workspace_bytes, stream);
+}
+
+extern "C" int vlc_linear_set_kernel(int mode) {
+  if (mode < 0 || mode > 2) return VLC_ERR_UNSUPPORTED;
+  g_kernel_mode.store(mode);
+  return VLC_OK;
 }

@@ -361,6 +361,12 @@ def linear_workspace(kind: int, m: int, n: int, k: int, device) -> tuple[torch.T
     return ws, ws.numel()
 
 
+def set_linear_kernel(mode: int) -> None:
+    """GEMM kernel of the linear ops, process-wide: 0 automatic, 1 single-SM tiles (stream-K
+    where it pays), 2 CTA pairs (tcgen05.mma.cta_group::2)."""
+    check("vlc_linear_set_kernel", lib().vlc_linear_set_kernel(int(mode)))
+
+
 def reset_linear_workspaces() -> None:
     """Zero the cached stream-K workspaces (after a recorded device error)."""
     for ws in _LINEAR_WS.values():
