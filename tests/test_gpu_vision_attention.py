@@ -115,3 +115,31 @@ def test_causal_contiguous_head_dim_80_and_clipped_stores(cuda_lib, margins):
     assert int(wide[:, H * d:].abs().sum()) == 0
     ref = oatt.varlen_attention(q.cpu(), k.cpu(), v.cpu(), cq, ck, scale, causal=True)
     _check(margins, "causal contiguous d=80 kernel vs oracle", out, ref)
+
+
+@pytest.mark.parametrize("H,Hk,d,maxlen", [(16, 16, 80, 128), (16, 2, 128, 16)])
+def test_packed_short_sequences(cuda_lib, margins, H, Hk, d, maxlen):
+    """Non-causal self-attention of short sequences of random lengths 1..maxlen (whole
+    sequences packed several to a tile, block-diagonal mask), GQA included: kernel vs oracle
+    on every row and vs flash-attn."""
+    from vlcache_b200.layers.vision_attention import varlen_attention
+    rng = np.random.default_rng(d + maxlen)
+    lens = rng.integers(1, maxlen + 1, size=300).tolist()
+    cu = _cu(lens)
+    n = int(cu[-1])
+    g = torch.Generator(device="cuda").manual_seed(17)
+    q = torch.randn(n, H, d, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(n, Hk, d, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(n, Hk, d, generator=g, device="cuda").to(torch.bfloat16)
+    scale = 1.0 / math.sqrt(d)
+    cu_d = torch.from_numpy(cu).cuda()
+    out = varlen_attention(q, k, v, cu_d, cu_d, max(lens), max(lens), scale, cu_seqlens_q_host=cu,
+                           cu_seqlens_k_host=cu)
+    torch.cuda.synchronize()
+    from vlcache_b200 import ops
+    assert ops.device_error() == 0
+    ref = oatt.varlen_attention(q.cpu(), k.cpu(), v.cpu(), cu, cu, scale, causal=False)
+    _check(margins, f"packed sequences H={H} Hk={Hk} d={d} kernel vs oracle", out, ref)
+    fa = pytest.importorskip("flash_attn")
+    fo = fa.flash_attn_varlen_func(q, k, v, cu_d, cu_d, max(lens), max(lens), softmax_scale=scale, causal=False)
+    _check(margins, f"packed sequences H={H} Hk={Hk} d={d} kernel vs flash-attn", out, fo)

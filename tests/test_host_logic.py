@@ -249,3 +249,34 @@ def test_cache_budget_matches_reference_rule():
     assert b.num_encoder_blocks == int(available * 0.2) // enc_block
     with pytest.raises(ValueError):
         kvc.cache_budget(36, 2, 128, 2048, mem_info=(1 * GiB, 180 * GiB), peak_bytes=0, current_bytes=0)
+
+
+@pytest.mark.parametrize("H,Hk,lens", [(16, 16, [64, 64, 37, 64, 16, 1, 64, 48, 128]),
+                                        (16, 2, [16, 3, 16, 9, 7, 16, 1])])
+def test_planner_packs_short_noncausal_sequences(H, Hk, lens):
+    """Non-causal self-attention of sequences that fit a tile (vision windows) packs whole
+    consecutive sequences into single-block tiles; every token is in exactly one tile per
+    KV head, and the plan's segment table gives each token its sequence's bounds."""
+    from vlcache_b200 import ops
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    plan = ops.build_prefill_plan(cu, cu, H, Hk, 128, num_sms=8, causal=False)
+    grid, cta, units, merges, nparts = _decode_plan(plan)
+    T = 128 // (H // Hk)
+    assert nparts == 0 and len(merges) == 0
+    seen = np.zeros((int(cu[-1]), Hk), np.int32)
+    starts = set(cu[:-1].tolist())
+    for u in units:
+        assert int(u[0]) == -1 and int(u[12]) == 0 and int(u[3]) - int(u[2]) == 1   # single, one block
+        q0, qc = int(u[7]), int(u[8])
+        assert 0 < qc <= T and q0 in starts and (q0 + qc) in set(cu.tolist())   # whole sequences
+        assert int(u[4]) == qc and int(u[5]) == q0 and int(u[9]) == -1
+        seen[q0:q0 + qc, int(u[1])] += 1
+    assert np.all(seen == 1)
+    off = int(plan.host[20])
+    seg = plan.host[off:off + 2 * int(cu[-1])].reshape(-1, 2)
+    for b in range(len(lens)):
+        assert np.all(seg[cu[b]:cu[b + 1]] == [cu[b], cu[b + 1]])
+    # a causal plan, or one with a sequence longer than a tile, is not packed
+    assert int(ops.build_prefill_plan(cu, cu, H, Hk, 128, num_sms=8, causal=True).host[20]) == 0
+    longer = np.array([0, T + 1], np.int32)
+    assert int(ops.build_prefill_plan(longer, longer, H, Hk, 128, num_sms=8, causal=False).host[20]) == 0

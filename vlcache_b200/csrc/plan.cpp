@@ -84,6 +84,43 @@ void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num
   }
 }
 
+// Non-causal self-attention whose sequences all fit a tile (the vision tower's windows):
+// consecutive whole sequences are packed into tiles of at most T tokens.
+bool packable(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int T, bool causal) {
+  if (causal || num_seqs <= 0) return false;
+  for (int b = 0; b <= num_seqs; ++b)
+    if (cu_q[b] != cu_k[b]) return false;
+  for (int b = 0; b < num_seqs; ++b)
+    if (cu_q[b + 1] - cu_q[b] > T) return false;
+  return true;
+}
+
+void build_packed_tiles(const int32_t* cu_q, int num_seqs, int num_kv_heads, int T, std::vector<Tile>& tiles) {
+  for (int g = 0; g < num_kv_heads; ++g) {
+    int b = 0;
+    while (b < num_seqs) {
+      if (cu_q[b + 1] == cu_q[b]) {
+        ++b;
+        continue;
+      }
+      const int q0 = cu_q[b];
+      int e = b;
+      while (e < num_seqs && cu_q[e + 1] - q0 <= T) ++e;
+      Tile t;
+      t.seq = -1;
+      t.kv_head = g;
+      t.q_begin = q0;
+      t.q_count = cu_q[e] - q0;
+      t.kpos0 = -1;  // the kernel masks every block of a packed tile by the row's sequence
+      t.n_kb = 1;
+      t.kv_len = t.q_count;
+      t.k_base = q0;
+      tiles.push_back(t);
+      b = e;
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" int64_t vlc_attention_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
@@ -93,12 +130,16 @@ extern "C" int64_t vlc_attention_plan_capacity(const int32_t* cu_q, const int32_
   const int G = num_heads / num_kv_heads;
   const int T = kTileRows / G;
   std::vector<Tile> tiles;
-  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
+  const bool packed = packable(cu_q, cu_k, num_seqs, T, causal != 0);
+  if (packed)
+    build_packed_tiles(cu_q, num_seqs, num_kv_heads, T, tiles);
+  else
+    build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
   int64_t total_kb = 0;
   for (const Tile& t : tiles) total_kb += t.n_kb;
   const int64_t max_units = (int64_t)tiles.size() + total_kb;
   return vlc::kPlanHeaderInts + (num_sms + 1) + max_units * vlc::kUnitInts +
-         (int64_t)tiles.size() * (vlc::kMergeInts + kTileRows);
+         (int64_t)tiles.size() * (vlc::kMergeInts + kTileRows) + (packed ? 2LL * cu_q[num_seqs] : 0);
 }
 
 extern "C" int64_t vlc_prefill_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
@@ -117,7 +158,11 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   const int G = num_heads / num_kv_heads;
   const int T = kTileRows / G;
   std::vector<Tile> tiles;
-  build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
+  const bool packed = packable(cu_q, cu_k, num_seqs, T, causal != 0);
+  if (packed)
+    build_packed_tiles(cu_q, num_seqs, num_kv_heads, T, tiles);
+  else
+    build_tiles(cu_q, cu_k, num_seqs, num_kv_heads, T, causal != 0, tiles);
 
   // Pair the tiles of each (sequence, KV head) from the end: (last, second last),
   // ...; with an odd count the first (cheapest) tile stays alone.  The later tile
@@ -129,7 +174,10 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   pairs.reserve(tiles.size());
   for (size_t i = 0; i < tiles.size();) {
     size_t e = i;
-    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head) ++e;
+    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head &&
+           tiles[i].seq >= 0)  // packed tiles have keys of their own: never paired
+      ++e;
+    if (e == i) e = i + 1;
     int last = (int)e - 1;
     while (last >= (int)i) {
       if (last - 1 >= (int)i) {
@@ -347,7 +395,8 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
     for (int r0 = 0; r0 < merges[i][kMRows]; r0 += rpb) merge_blocks.push_back((int32_t)((i << 8) | r0));
   }
   const int64_t off_mblocks = off_merges + (int64_t)merges.size() * kMergeInts;
-  const int64_t total = off_mblocks + (int64_t)merge_blocks.size();
+  const int64_t off_segments = packed ? off_mblocks + (int64_t)merge_blocks.size() : 0;
+  const int64_t total = off_mblocks + (int64_t)merge_blocks.size() + (packed ? 2LL * cu_q[num_seqs] : 0);
   if (total > plan_capacity) return VLC_ERR_PLAN;
 
   int32_t* h = plan_out;
@@ -372,6 +421,15 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   h[kPOffMergeBlocks] = (int32_t)off_mblocks;
   h[kPCausal] = causal != 0 ? 1 : 0;
   h[kPHeadDim] = head_dim;
+  h[kPOffSegments] = (int32_t)off_segments;
+  if (packed) {
+    int32_t* seg = h + off_segments;
+    for (int b = 0; b < num_seqs; ++b)
+      for (int t = cu_q[b]; t < cu_q[b + 1]; ++t) {
+        seg[2 * (int64_t)t] = cu_q[b];
+        seg[2 * (int64_t)t + 1] = cu_q[b + 1];
+      }
+  }
   int32_t* cta = h + off_cta;
   int32_t* up = h + off_units;
   for (int c = 0; c <= grid; ++c) cta[c] = cta_begin[c];

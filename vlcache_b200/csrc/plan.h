@@ -8,8 +8,8 @@
 namespace vlc {
 
 constexpr int32_t kPlanMagic = 0x564C4350;  // 'VLCP'
-constexpr int32_t kPlanVersion = 5;
-constexpr int kPlanHeaderInts = 20;
+constexpr int32_t kPlanVersion = 6;
+constexpr int kPlanHeaderInts = 24;
 
 // header fields
 enum : int {
@@ -33,6 +33,8 @@ enum : int {
   kPOffMergeBlocks = 17,  // int32[merge_blocks]: (merge index << 8) | first row of the block
   kPCausal = 18,          // 1: row i of a sequence sees keys <= k_len - q_len + i; 0: all k_len keys
   kPHeadDim = 19,         // head_dim the plan was made for (64 < d <= 128, d % 16 == 0)
+  kPOffSegments = 20,     // 0, or int32[total_q][2]: {first, end} token of each query token's
+                          // sequence, for packed tiles (several short sequences in one tile)
 };
 
 // A unit is one or two query tiles of one (sequence, KV head) over one range of
@@ -40,9 +42,13 @@ enum : int {
 // tokens and covers blocks [kb_begin, kb_end) (at least one); tile B, when
 // present (kUQCountB > 0), holds earlier tokens of the same sequence and covers
 // [kb_begin, kb_end_b) with kb_begin < kb_end_b <= kb_end.
+// Packed tile (kUSeq == -1, non-causal self-attention of short sequences, contiguous K/V
+// only): tile A holds whole consecutive sequences, tokens [q_begin, q_begin + q_count); its one
+// key block is the same tokens (k_base = q_begin, kv_len = q_count), and row t sees the keys of
+// its own sequence, [segments[t][0], segments[t][1]).
 constexpr int kUnitInts = 16;
 enum : int {
-  kUSeq = 0,       // row of block_tables
+  kUSeq = 0,       // row of block_tables (-1: packed tile)
   kUKvHead = 1,
   kUKbBegin = 2,   // first 128-key block (both tiles)
   kUKbEnd = 3,     // one past the last block of tile A

@@ -100,6 +100,7 @@ struct Params {
   int tokens_per_tile;  // T
   int head_dim;         // d of q/k/v/out (64 < d <= 128); tiles are zero-padded to 128 columns
   int causal;           // 0: every row sees all of its sequence's keys
+  const int32_t* segments;  // packed plans: {first, end} token of each query token's sequence
   __nv_bfloat16* out;
   int64_t out_token_stride;
   int out_store32;        // out rows are 32-byte aligned: 256-bit stores
@@ -507,7 +508,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       const int part = u[x == 0 ? kUPartA : kUPartB];
       const int tok = row / p.group;
       const bool row_valid = row < p.rows && tok < q_count;
-      const int qpos = p.causal ? kpos0 + tok : kpos0;  // non-causal: kpos0 = k_len - 1
+      // The row sees keys [row_lo, row_hi) of the unit's key space: causal, [0, qpos]; not
+      // causal, all k_len (kpos0 = k_len - 1); a packed tile (several short sequences, one key
+      // block = the same tokens, kpos0 = -1 so every block is masked) its own sequence's, and
+      // rows past q_count none.
+      int row_lo = 0, row_hi = (p.causal ? kpos0 + tok : kpos0) + 1;
+      if (u[kUSeq] < 0) {
+        row_lo = row_hi = 0;
+        if (row_valid) {
+          const int k_base = u[kUKBase];
+          row_lo = __ldg(p.segments + 2 * (int64_t)(q_begin + tok)) - k_base;
+          row_hi = __ldg(p.segments + 2 * (int64_t)(q_begin + tok) + 1) - k_base;
+        }
+      }
       float m_use = -INFINITY;
       float l_row = 0.f;
       bool ok = true;
@@ -523,11 +536,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld32(s_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[q * 32]));
         tmem_wait_ld();
-        if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal
-          const int lim = qpos - key0;
+        if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal (or a packed tile)
+          const int lo = row_lo - key0, hi = row_hi - key0;
 #pragma unroll
           for (int c = 0; c < 128; ++c)
-            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+            if (c < lo || c >= hi) sr[c] = __float_as_uint(-INFINITY);
         }
         float mx[8];
 #pragma unroll
@@ -923,6 +936,8 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   prm.tokens_per_tile = T;
   prm.head_dim = head_dim;
   prm.causal = plan_host[kPCausal];
+  prm.segments = plan_host[kPOffSegments] > 0 ? plan_dev + plan_host[kPOffSegments] : nullptr;
+  if (prm.segments != nullptr && block_tables != nullptr) return VLC_ERR_PLAN;  // packed tiles: contiguous K/V
 
   static std::atomic<uint64_t> smem_set{0};
   if (ensure_dynamic_smem((const void*)prefill_attn_kernel, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
