@@ -269,7 +269,7 @@ def test_planner_packs_short_noncausal_sequences(H, Hk, lens):
         assert int(u[0]) == -1 and int(u[12]) == 0 and int(u[3]) - int(u[2]) == 1   # single, one block
         q0, qc = int(u[7]), int(u[8])
         assert 0 < qc <= T and q0 in starts and (q0 + qc) in set(cu.tolist())   # whole sequences
-        assert int(u[4]) == qc and int(u[5]) == q0 and int(u[9]) == -1
+        assert int(u[4]) == qc and int(u[5]) == q0
         seen[q0:q0 + qc, int(u[1])] += 1
     assert np.all(seen == 1)
     off = int(plan.host[20])

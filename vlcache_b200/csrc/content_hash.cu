@@ -15,8 +15,9 @@
 // (n1 = number of level-1 chunks, 0 for empty data; header = the caller's bytes, e.g.
 // grid_thw, at most 256.)  The keys are used only inside one engine process, so any
 // strong 64-bit content hash keeps the reference's behaviour: same bytes, same key.
-// The GPU path is HBM-bound (one thread per 1 KB chunk, 16-byte loads); the host path
-// splits level 1 over threads.  Both give the same digest for the same bytes.
+// The GPU path: level 1 stages each block's chunks in shared memory with bulk copies and
+// hashes one chunk per thread; level 2 and the digest follow.  The host path splits level 1
+// over threads.  Both give the same digest for the same bytes.
 #include <algorithm>
 #include <cstring>
 #include <thread>
@@ -175,6 +176,46 @@ __global__ void __launch_bounds__(256) hash_chunks_kernel(const uint8_t* __restr
   out[i] = avalanche(h);  // a full chunk leaves no tail
 }
 
+// Level 1, staged: a block's 64 full chunks come into shared memory with one 1 KB bulk copy
+// each (the copy engine streams whole chunks; a lane-per-chunk global read would touch 32
+// lines per warp access), rows padded to 1,040 bytes so that the 8 lanes of a 16-byte
+// shared-memory access hit distinct banks; then thread i hashes chunk i from shared memory.
+// The waits are bounded (a timeout records a device error and the block returns).
+constexpr int kStageChunks = 64;
+constexpr int kStageRow = kChunk + 16;
+constexpr int kStageSmem = kStageChunks * kStageRow + 64;
+__global__ void __launch_bounds__(kStageChunks) hash_chunks_staged_kernel(const uint8_t* __restrict__ data,
+                                                                          uint64_t* __restrict__ out,
+                                                                          int64_t full_chunks, uint64_t seed) {
+  extern __shared__ __align__(128) uint8_t stage[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(stage + kStageChunks * kStageRow);
+  const int64_t c0 = (int64_t)blockIdx.x * kStageChunks;
+  const int n = (int)min((int64_t)kStageChunks, full_chunks - c0);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(bar, (uint32_t)(n * kChunk));
+    for (int i = 0; i < n; ++i) bulk_load_1d(stage + i * kStageRow, data + (c0 + i) * kChunk, kChunk, bar);
+  }
+  if (!mbar_wait_bounded(bar, 0, VLC_DEV_ERR_TIMEOUT + 50, VLC_WAIT_LIMIT_CYCLES)) return;
+  const int i = threadIdx.x;
+  if (i >= n) return;
+  uint64_t v1 = seed + P1 + P2, v2 = seed + P2, v3 = seed, v4 = seed - P1;
+  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(stage + i * kStageRow);
+#pragma unroll 8
+  for (int s = 0; s < kChunk / 32; ++s) {
+    const ulonglong2 a = q[2 * s], b = q[2 * s + 1];
+    v1 = xround(v1, a.x);
+    v2 = xround(v2, a.y);
+    v3 = xround(v3, b.x);
+    v4 = xround(v4, b.y);
+  }
+  out[c0 + i] = avalanche(xstripes_done(v1, v2, v3, v4) + (uint64_t)kChunk);
+}
+
 struct Header {
   uint8_t bytes[kMaxHeader];
   int len;
@@ -278,10 +319,29 @@ extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const v
   if (n1 > 0) {
     const int64_t blocks = (n1 + 255) / 256;
     if (blocks > 0x7fffffff) return VLC_ERR_SHAPE;
-    hash_chunks_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint8_t*)data, nbytes, d1, n1, 1,
-                                                         aligned16(data) ? 1 : 0);
-    int rc = launch_status();
-    if (rc != VLC_OK) return rc;
+    int rc;
+    const int64_t full = nbytes / kChunk;
+    if (aligned16(data) && full > 0) {
+      // full chunks staged through shared memory; the shorter last chunk on its own
+      static std::atomic<uint64_t> staged_set{0};
+      if (ensure_dynamic_smem((const void*)hash_chunks_staged_kernel, kStageSmem, staged_set) != VLC_OK)
+        return VLC_ERR_CUDA;
+      hash_chunks_staged_kernel<<<(unsigned)((full + kStageChunks - 1) / kStageChunks), kStageChunks, kStageSmem,
+                                  st>>>((const uint8_t*)data, d1, full, 1);
+      rc = launch_status();
+      if (rc != VLC_OK) return rc;
+      if (full < n1) {
+        hash_chunks_kernel<<<1, 32, 0, st>>>((const uint8_t*)data + full * kChunk, nbytes - full * kChunk,
+                                             d1 + full, 1, 1, 0);
+        rc = launch_status();
+        if (rc != VLC_OK) return rc;
+      }
+    } else {
+      hash_chunks_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint8_t*)data, nbytes, d1, n1, 1,
+                                                           aligned16(data) ? 1 : 0);
+      rc = launch_status();
+      if (rc != VLC_OK) return rc;
+    }
     hash_level2_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(d1, n1, d2, n2);
     rc = launch_status();
     if (rc != VLC_OK) return rc;

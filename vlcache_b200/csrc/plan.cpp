@@ -111,7 +111,7 @@ void build_packed_tiles(const int32_t* cu_q, int num_seqs, int num_kv_heads, int
       t.kv_head = g;
       t.q_begin = q0;
       t.q_count = cu_q[e] - q0;
-      t.kpos0 = -1;  // the kernel masks every block of a packed tile by the row's sequence
+      t.kpos0 = 0;  // unused: the packed kernel masks by the row's sequence
       t.n_kb = 1;
       t.kv_len = t.q_count;
       t.k_base = q0;

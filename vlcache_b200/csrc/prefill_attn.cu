@@ -207,6 +207,9 @@ __device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, 
   }
 }
 
+// kPacked: the plan packs several short sequences per tile (block-diagonal mask); a separate
+// instantiation, so the causal path's code is not touched by it.
+template <bool kPacked>
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -508,19 +511,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       const int part = u[x == 0 ? kUPartA : kUPartB];
       const int tok = row / p.group;
       const bool row_valid = row < p.rows && tok < q_count;
-      // The row sees keys [row_lo, row_hi) of the unit's key space: causal, [0, qpos]; not
-      // causal, all k_len (kpos0 = k_len - 1); a packed tile (several short sequences, one key
-      // block = the same tokens, kpos0 = -1 so every block is masked) its own sequence's, and
-      // rows past q_count none.
-      int row_lo = 0, row_hi = (p.causal ? kpos0 + tok : kpos0) + 1;
-      if (u[kUSeq] < 0) {
-        row_lo = row_hi = 0;
-        if (row_valid) {
-          const int k_base = u[kUKBase];
-          row_lo = __ldg(p.segments + 2 * (int64_t)(q_begin + tok)) - k_base;
-          row_hi = __ldg(p.segments + 2 * (int64_t)(q_begin + tok) + 1) - k_base;
-        }
-      }
+      const int qpos = p.causal ? kpos0 + tok : kpos0;  // non-causal: kpos0 = k_len - 1
+
       float m_use = -INFINITY;
       float l_row = 0.f;
       bool ok = true;
@@ -536,11 +528,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld32(s_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[q * 32]));
         tmem_wait_ld();
-        if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal (or a packed tile)
-          const int lo = row_lo - key0, hi = row_hi - key0;
+        if (kPacked) {
+          // Packed tile (several short sequences, one key block = the same tokens): the row
+          // sees keys [lo, hi) of the block, its own sequence's; rows past q_count none.
+          int lo = 0, hi = 0;
+          if (row_valid) {
+            const int k_base = p.units[(int64_t)ui * kUnitInts + kUKBase];
+            lo = __ldg(p.segments + 2 * (int64_t)(q_begin + tok)) - k_base;
+            hi = __ldg(p.segments + 2 * (int64_t)(q_begin + tok) + 1) - k_base;
+          }
 #pragma unroll
           for (int c = 0; c < 128; ++c)
             if (c < lo || c >= hi) sr[c] = __float_as_uint(-INFINITY);
+        } else if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal
+          const int lim = qpos - key0;
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
         }
         float mx[8];
 #pragma unroll
@@ -939,8 +943,11 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   prm.segments = plan_host[kPOffSegments] > 0 ? plan_dev + plan_host[kPOffSegments] : nullptr;
   if (prm.segments != nullptr && block_tables != nullptr) return VLC_ERR_PLAN;  // packed tiles: contiguous K/V
 
-  static std::atomic<uint64_t> smem_set{0};
-  if (ensure_dynamic_smem((const void*)prefill_attn_kernel, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
+  const bool packed = prm.segments != nullptr;
+  static std::atomic<uint64_t> smem_set{0}, smem_set_packed{0};
+  if (ensure_dynamic_smem(packed ? (const void*)prefill_attn_kernel<true> : (const void*)prefill_attn_kernel<false>,
+                          SMEM_BYTES, packed ? smem_set_packed : smem_set) != VLC_OK)
+    return VLC_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   // Both kernels are launched as programmatic dependents of their predecessor in the
   // stream (the attention: of the KV scatter; the merge: of the attention).  They wait
@@ -956,7 +963,9 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
   cfg.stream = st;
   cfg.attrs = &pdl;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel, prm) != cudaSuccess) {
+  const cudaError_t le = packed ? cudaLaunchKernelEx(&cfg, prefill_attn_kernel<true>, prm)
+                                : cudaLaunchKernelEx(&cfg, prefill_attn_kernel<false>, prm);
+  if (le != cudaSuccess) {
     (void)cudaGetLastError();
     return VLC_ERR_CUDA;
   }
