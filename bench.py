@@ -199,9 +199,12 @@ class WarmPrefillWorkload:
     def v(self, l):
         return self.qkv[l, :, (H + HK) * D:].view(self.total_q, HK, D)
 
-    def attention(self, l):
+    def attention(self, l, inflight=False):
+        # inflight: the first sub-sequence (keys == its own recomputed rows) reads K/V from
+        # the projection's rows and does not wait for the scatter launched just before
         self.ops.prefill_attention(self.q(l), self.kv_cache[0, l], self.kv_cache[1, l], self.block_tables, self.plan,
-                                   self.scale, self.out[l], self.ws)
+                                   self.scale, self.out[l], self.ws,
+                                   k_new=self.k(l) if inflight else None, v_new=self.v(l) if inflight else None)
 
     def step(self):
         # Layer l's reused image rows are re-placed (moved + M-RoPE shifted) on a
@@ -213,7 +216,7 @@ class WarmPrefillWorkload:
             # successor, so its programmatic launch overlaps the scatter)
             cur.wait_event(ready[l])
             self.ops.store_kvcache(self.k(l), self.v(l), self.kv_cache[0, l], self.kv_cache[1, l], self.slot_mapping)
-            self.attention(l)
+            self.attention(l, inflight=True)
         cur.wait_stream(self.side)
 
     def attention_only(self):

@@ -185,6 +185,26 @@ int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num
                      void* out, int64_t out_token_stride, void* workspace,
                      int64_t workspace_bytes, void* stream);
 
+/* Same as vlc_prefill_attn, plus the step's in-flight K/V: k_new / v_new hold the
+ * rows the projection produced for the queries ([num_new_rows >= total_q, num_kv_heads,
+ * head_dim], row strides kn_row_stride / vn_row_stride; row i is the key / value of query
+ * row i, before store_kvcache copies it into the cache).  A sequence whose q_len equals
+ * its k_len attends over exactly its own rows (a warm request's first sub-sequence:
+ * model_runner.py:237-242 builds Q = K = tokens [0, img_start + R)), so its keys are read
+ * from these rows instead of the cache and its work does not wait for the kernel
+ * launched just before; the other sequences' K/V loads do.  That kernel may only write
+ * the paged cache (the KV scatter), and must be an ordinary stream-ordered launch: q,
+ * k_new, v_new complete and out / workspace free when it starts. */
+int vlc_prefill_attn_inflight(const void* q, int64_t q_token_stride, int total_q, int num_heads,
+                              const void* k, const void* v, int64_t k_row_stride, int64_t v_row_stride,
+                              int64_t num_kv_rows, int num_kv_heads, int head_dim,
+                              const int32_t* block_tables, int block_table_stride, int block_size,
+                              const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
+                              void* out, int64_t out_token_stride, void* workspace,
+                              int64_t workspace_bytes, const void* k_new, const void* v_new,
+                              int64_t kn_row_stride, int64_t vn_row_stride, int64_t num_new_rows,
+                              void* stream);
+
 /* --------------------------------------------------------------------------
  * Split-K paged flash-decode.
  * Replaces flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,

@@ -189,6 +189,59 @@ def test_prefill_split_tiles_repeat_launches(ops):
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
 
 
+def _inflight_rows(case, H, Hk):
+    """k_new / v_new as the projection would hold them: row i = key / value of query row i
+    (gathered from the pages through the block table)."""
+    bs = case.k_cache.shape[1]
+    bt = case.block_tables.cpu().numpy()
+    slots = []
+    for b in range(len(case.cu_q) - 1):
+        ql, kl = case.cu_q[b + 1] - case.cu_q[b], case.cu_k[b + 1] - case.cu_k[b]
+        for t in range(ql):
+            pos = kl - ql + t
+            slots.append(int(bt[b][pos // bs]) * bs + pos % bs)
+    idx = torch.tensor(slots, device=case.k_cache.device)
+    D = case.k_cache.shape[-1]
+    return case.k_cache.view(-1, Hk, D)[idx].contiguous(), case.v_cache.view(-1, Hk, D)[idx].contiguous()
+
+
+def test_prefill_inflight_kv(ops):
+    """vlc_prefill_attn_inflight: the first sub-sequence of each warm request (q_len ==
+    k_len) reads its keys from the in-flight rows.  Its pages are replaced by NaN copies
+    (a second block-table row), so the paged launch would fail there; the in-flight launch
+    gives bit-for-bit the paged launch on the intact cache, split tiles included."""
+    H, Hk = 16, 2
+    case = make_warm_case([(16, 1024, 32, 102), (5, 2000, 17, 300), (0, 400, 9, 40)], H, Hk, device="cuda",
+                          seed=31)
+    plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, Hk, device="cuda", num_sms=32)
+    assert plan.num_merges > 0
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device="cuda")
+    ref = ops.prefill_attention(case.q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale,
+                                workspace=ws)
+    k_new, v_new = _inflight_rows(case, H, Hk)
+    # NaN copies of every page the self-attention rows use, referenced only by their rows
+    bt = case.block_tables.clone()
+    nb = case.k_cache.shape[0]
+    extra = []
+    for b in range(len(case.cu_q) - 1):
+        if case.cu_q[b + 1] - case.cu_q[b] != case.cu_k[b + 1] - case.cu_k[b]:
+            continue
+        for j in range(bt.shape[1]):
+            if int(bt[b, j]) >= 0:
+                extra.append(int(bt[b, j]))
+                bt[b, j] = nb + len(extra) - 1
+    assert extra
+    nan_pages = torch.full((len(extra),) + tuple(case.k_cache.shape[1:]), float("nan"), dtype=torch.bfloat16,
+                           device="cuda")
+    kc = torch.cat([case.k_cache, nan_pages])
+    vc = torch.cat([case.v_cache, nan_pages])
+    out = ops.prefill_attention(case.q, kc, vc, bt, plan, case.scale, workspace=ws, k_new=k_new, v_new=v_new)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.isfinite(out.float()).all()
+    assert torch.equal(out, ref)
+
+
 def test_prefill_cfg2_full_size(ops):
     """BASELINE config 2 (3B, 4K image, 10% recompute): 1,123 query rows x 10,617 keys."""
     H, Hk = 16, 2

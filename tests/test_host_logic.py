@@ -55,7 +55,7 @@ def test_recompute_count():
 
 
 # ---------------------------------------------------------------- planner (C ABI, host only)
-UNIT_INTS, MERGE_INTS = 16, 8
+UNIT_INTS, MERGE_INTS = 17, 8
 
 
 def _decode_plan(plan):
@@ -97,9 +97,12 @@ def _coverage(cu_q, cu_k, H, Hk, num_sms, causal=True, head_dim=128):
                 for kb in range(pos // 128 + 1):
                     need[(cu_q[b] + t, g, kb)] = 0
     parts_seen = set()
+    # self-attention sequences (q_len == k_len) name their first row (in-flight K/V)
     for u in units:
         seq, g = int(u[0]), int(u[1])
         assert int(u[4]) == cu_k[seq + 1] - cu_k[seq] and int(u[5]) == cu_k[seq]
+        ql, kl = cu_q[seq + 1] - cu_q[seq], cu_k[seq + 1] - cu_k[seq]
+        assert int(u[16]) == (cu_q[seq] if ql == kl else -1)
         tiles = _unit_tiles(u)
         assert tiles[0][5] > tiles[0][4]                    # tile A always has work
         if len(tiles) == 2:

@@ -38,6 +38,9 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_prefill_workspace_size": (c_i64, [c_vp]),
     "vlc_prefill_attn": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int,
                                  c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_i64, c_vp, c_i64, c_vp]),
+    "vlc_prefill_attn_inflight": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int,
+                                          c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_i64, c_vp, c_i64,
+                                          c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "vlc_decode_attn": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_int, c_int, c_vp, c_int,
                                 c_int, c_vp, c_int, c_float, c_vp, c_i64, c_vp, c_i64, c_vp]),
     "vlc_decode_workspace_size": (c_i64, [c_int, c_int, c_int, c_int]),

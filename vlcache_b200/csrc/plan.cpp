@@ -32,6 +32,7 @@ constexpr int kMaxParts = 20;
 
 struct Tile {
   int seq, kv_head, q_begin, q_count, kpos0, n_kb, kv_len, k_base;
+  int self_row;  // cu_q[seq] when q_len == k_len, else -1
 };
 
 struct UnitRec {
@@ -78,6 +79,7 @@ void build_tiles(const int32_t* cu_q, const int32_t* cu_k, int num_seqs, int num
         t.n_kb = max_pos / kBlockN + 1;
         t.kv_len = kl;
         t.k_base = cu_k[b];
+        t.self_row = ql == kl ? cu_q[b] : -1;
         tiles.push_back(t);
       }
     }
@@ -115,6 +117,7 @@ void build_packed_tiles(const int32_t* cu_q, int num_seqs, int num_kv_heads, int
       t.n_kb = 1;
       t.kv_len = t.q_count;
       t.k_base = q0;
+      t.self_row = -1;  // packed tiles read contiguous K/V only
       tiles.push_back(t);
       b = e;
     }
@@ -334,6 +337,7 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
       u.f[kUKbEnd] = kb1;
       u.f[kUKvLen] = ta.kv_len;
       u.f[kUKBase] = ta.k_base;
+      u.f[kUSelfRow] = ta.self_row;
       u.f[kUQBeginA] = ta.q_begin;
       u.f[kUQCountA] = ta.q_count;
       u.f[kUKpos0A] = ta.kpos0;
@@ -376,7 +380,9 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
       heap.push(l);
     }
   }
-  // Units grouped by CTA (counting sort, LPT order inside a CTA).
+  // Units grouped by CTA (counting sort, LPT order inside a CTA).  (Putting the
+  // self-attention units first, so that with in-flight K/V they run while the scatter
+  // finishes, measured slower: the LPT order's tail matters more.)
   std::vector<int> cta_begin(grid + 1, 0), by_cta(num_units);
   for (int i = 0; i < num_units; ++i) ++cta_begin[cta_of[i] + 1];
   for (int c = 0; c < grid; ++c) cta_begin[c + 1] += cta_begin[c];

@@ -8,7 +8,7 @@
 namespace vlc {
 
 constexpr int32_t kPlanMagic = 0x564C4350;  // 'VLCP'
-constexpr int32_t kPlanVersion = 6;
+constexpr int32_t kPlanVersion = 7;
 constexpr int kPlanHeaderInts = 24;
 
 // header fields
@@ -46,7 +46,7 @@ enum : int {
 // only): tile A holds whole consecutive sequences, tokens [q_begin, q_begin + q_count); its one
 // key block is the same tokens (k_base = q_begin, kv_len = q_count), and row t sees the keys of
 // its own sequence, [segments[t][0], segments[t][1]).
-constexpr int kUnitInts = 16;
+constexpr int kUnitInts = 17;
 enum : int {
   kUSeq = 0,       // row of block_tables (-1: packed tile)
   kUKvHead = 1,
@@ -64,6 +64,9 @@ enum : int {
   kUKpos0B = 13,
   kUPartB = 14,
   kUKbEndB = 15,   // one past tile B's last block
+  kUSelfRow = 16,  // q_len == k_len (the sequence attends over its own rows): the row of its
+                   // first token in q, which is also its first key row in the in-flight K/V
+                   // (the projection's output); -1 otherwise
 };
 
 // merge fields (one record per split query tile)

@@ -106,6 +106,12 @@ struct Params {
   int out_store32;        // out rows are 32-byte aligned: 256-bit stores
   __nv_bfloat16* part_o;  // [num_parts][BM][HD] partial O / l (bf16)
   float* part_ml;         // [num_parts][BM][2]  (max in log2 domain, sum)
+  // In-flight K/V (the projection's rows, dims {d, Hk, num_new_rows}, box {64, 1, BN}).
+  // inflight == 1: units of self-attention sequences (kUSelfRow >= 0) load their keys from
+  // here, and only the other units' K/V loads wait for the kernel launched just before.
+  CUtensorMap tm_kn;
+  CUtensorMap tm_vn;
+  int inflight;
 };
 
 struct Bars {
@@ -164,13 +170,20 @@ __device__ __forceinline__ UnitView unit_view(const int32_t* u) {
   return v;
 }
 
-// Row (slot) of the first key of 128-key block `kb` of a unit.  Paged mode
-// (block_tables != NULL, block_size % 128 == 0): through the block table.
-// Contiguous mode (block_tables == NULL): key rows of the sequence start at k_base.
+__device__ __forceinline__ bool unit_inflight(const Params& p, const int32_t* u) {
+  return p.inflight && u[kUSelfRow] >= 0;
+}
+
+// Row (slot) of the first key of 128-key block `kb` of a unit.  In-flight unit: rows of
+// the in-flight K/V from the sequence's first query row.  Paged mode (block_tables !=
+// NULL, block_size % 128 == 0): through the block table.  Contiguous mode (block_tables
+// == NULL): key rows of the sequence start at k_base.
 __device__ __forceinline__ int key_block_slot(const Params& p, const int32_t* u, int kb) {
   const int key0 = kb * BN;
   int64_t slot;
-  if (p.block_tables != nullptr) {
+  if (unit_inflight(p, u)) {
+    slot = (int64_t)u[kUSelfRow] + key0;  // box may run past the end: zero fill, masked
+  } else if (p.block_tables != nullptr) {
     const int page = __ldg(p.block_tables + (int64_t)u[kUSeq] * p.bt_stride + key0 / p.block_size);
     slot = (int64_t)page * p.block_size + (key0 % p.block_size);
     if (page < 0 || slot + BN > p.num_slots) {
@@ -250,6 +263,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    if (p.inflight) {
+      tma_prefetch_desc(&p.tm_kn);
+      tma_prefetch_desc(&p.tm_vn);
+    }
   }
   if (warp == 10 && lane == 0) {
     tma_prefetch_desc(&p.tm_q);
@@ -292,7 +309,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         q_b = u[kUQBeginB];
       };
       if (u_begin < u_end) fetch(u_begin);
-      pdl_wait();  // Q may be written by the preceding kernel
+      if (!p.inflight) pdl_wait();  // Q may be written by the preceding kernel
       int load = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         if (ui != u_begin) fetch(ui);
@@ -325,19 +342,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       // Plan and block tables are never written by the kernel launched just before:
       // the first unit's fields and its first page are read while the wait runs.
       int g = 0, kb0 = 0, kb1 = 0, slot0 = 0;
+      bool infl = false;
       const int32_t* u = nullptr;
       auto fetch = [&](int ui) {
         u = p.units + (int64_t)ui * kUnitInts;
         g = u[kUKvHead];
         kb0 = u[kUKbBegin];
         kb1 = u[kUKbEnd];
+        infl = unit_inflight(p, u);
         slot0 = kb0 < kb1 ? key_block_slot(p, u, kb0) : 0;
       };
       if (u_begin < u_end) fetch(u_begin);
-      pdl_wait();  // K/V rows are written by the preceding store_kvcache
+      bool waited = false;  // K/V rows (paged or contiguous) may be written by the preceding kernel
       int it = 0;
       for (int ui = u_begin; ui < u_end; ++ui) {
         if (ui != u_begin) fetch(ui);
+        if (!infl && !waited) {
+          pdl_wait();
+          waited = true;
+        }
+        const CUtensorMap* tk = infl ? &p.tm_kn : &p.tm_k;
+        const CUtensorMap* tv = infl ? &p.tm_vn : &p.tm_v;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
@@ -349,8 +374,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           }
           uint8_t* kdst = smem + OFF_K + s * TILE_BYTES;
           mbar_expect_tx(bars.k_full + s, TILE_BYTES);
-          tma_load_3d(kdst, &p.tm_k, bars.k_full + s, 0, g, slot);
-          tma_load_3d(kdst + HALF_BYTES, &p.tm_k, bars.k_full + s, 64, g, slot);
+          tma_load_3d(kdst, tk, bars.k_full + s, 0, g, slot);
+          tma_load_3d(kdst + HALF_BYTES, tk, bars.k_full + s, 64, g, slot);
           if (it >= STAGES && !wait_or_abort(bars.v_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 3, abort_flag)) {
             ok = false;
             break;
@@ -362,8 +387,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           }
           uint8_t* vdst = smem + OFF_V + s * TILE_BYTES;
           mbar_expect_tx(bars.v_full + s, TILE_BYTES);
-          tma_load_3d(vdst, &p.tm_v, bars.v_full + s, 0, g, slot);
-          tma_load_3d(vdst + HALF_BYTES, &p.tm_v, bars.v_full + s, 64, g, slot);
+          tma_load_3d(vdst, tv, bars.v_full + s, 0, g, slot);
+          tma_load_3d(vdst + HALF_BYTES, tv, bars.v_full + s, 64, g, slot);
         }
         if (!ok) break;
       }
@@ -856,13 +881,13 @@ extern "C" int64_t vlc_prefill_workspace_size(const int32_t* plan_host) {
   return parts * (int64_t)BM * (HD * (int64_t)sizeof(__nv_bfloat16) + 2 * (int64_t)sizeof(float));
 }
 
-extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num_heads,
-                                const void* k_cache, const void* v_cache, int64_t k_row_stride,
-                                int64_t v_row_stride, int64_t num_slots, int num_kv_heads, int head_dim,
-                                const int32_t* block_tables, int block_table_stride, int block_size,
-                                const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
-                                void* out, int64_t out_token_stride, void* workspace,
-                                int64_t workspace_bytes, void* stream) {
+static int prefill_attn_impl(const void* q, int64_t q_token_stride, int total_q, int num_heads, const void* k_cache,
+                             const void* v_cache, int64_t k_row_stride, int64_t v_row_stride, int64_t num_slots,
+                             int num_kv_heads, int head_dim, const int32_t* block_tables, int block_table_stride,
+                             int block_size, const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
+                             void* out, int64_t out_token_stride, void* workspace, int64_t workspace_bytes,
+                             const void* k_new, const void* v_new, int64_t kn_row_stride, int64_t vn_row_stride,
+                             int64_t num_new_rows, void* stream) {
   if (!q || !k_cache || !v_cache || !plan_dev || !plan_host || !out) return VLC_ERR_NULL;
   if (head_dim <= 64 || head_dim > HD || head_dim % 16 != 0) return VLC_ERR_UNSUPPORTED;
   if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return VLC_ERR_SHAPE;
@@ -881,6 +906,15 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
       k_row_stride < (int64_t)num_kv_heads * head_dim || v_row_stride < (int64_t)num_kv_heads * head_dim)
     return VLC_ERR_STRIDE;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) return VLC_ERR_ALIGN;
+  if ((k_new == nullptr) != (v_new == nullptr)) return VLC_ERR_NULL;
+  if (k_new != nullptr) {
+    // every self-attention sequence's keys are the in-flight rows of its queries
+    if (num_new_rows < total_q || num_new_rows > 0x7fffff00) return VLC_ERR_SHAPE;
+    if (kn_row_stride % 8 != 0 || vn_row_stride % 8 != 0 || kn_row_stride < (int64_t)num_kv_heads * head_dim ||
+        vn_row_stride < (int64_t)num_kv_heads * head_dim)
+      return VLC_ERR_STRIDE;
+    if (!aligned16(k_new) || !aligned16(v_new)) return VLC_ERR_ALIGN;
+  }
   const int64_t ws_need = vlc_prefill_workspace_size(plan_host);
   if (ws_need > 0 && (!workspace || workspace_bytes < ws_need)) return VLC_ERR_WORKSPACE;
   if (num_slots <= 0 || num_slots > 0x7fffff00) return VLC_ERR_SHAPE;
@@ -901,6 +935,18 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     const uint32_t box[3] = {64, 1, (uint32_t)BN};
     if (encode_tmap_bf16(&prm.tm_k, k_cache, 3, dims, ks, box, 128) != VLC_OK) return VLC_ERR_CUDA;
     if (encode_tmap_bf16(&prm.tm_v, v_cache, 3, dims, vs, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  }
+  prm.inflight = k_new != nullptr ? 1 : 0;
+  if (prm.inflight) {
+    const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_kv_heads, (uint64_t)num_new_rows};
+    const uint64_t ks[2] = {(uint64_t)head_dim * 2, (uint64_t)kn_row_stride * 2};
+    const uint64_t vs[2] = {(uint64_t)head_dim * 2, (uint64_t)vn_row_stride * 2};
+    const uint32_t box[3] = {64, 1, (uint32_t)BN};
+    if (encode_tmap_bf16(&prm.tm_kn, k_new, 3, dims, ks, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+    if (encode_tmap_bf16(&prm.tm_vn, v_new, 3, dims, vs, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+  } else {
+    prm.tm_kn = prm.tm_k;  // unused
+    prm.tm_vn = prm.tm_v;
   }
   {
     const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_heads, (uint64_t)total_q};
@@ -986,4 +1032,33 @@ extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total
     }
   }
   return rc;
+}
+
+extern "C" int vlc_prefill_attn(const void* q, int64_t q_token_stride, int total_q, int num_heads,
+                                const void* k_cache, const void* v_cache, int64_t k_row_stride,
+                                int64_t v_row_stride, int64_t num_slots, int num_kv_heads, int head_dim,
+                                const int32_t* block_tables, int block_table_stride, int block_size,
+                                const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
+                                void* out, int64_t out_token_stride, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  return prefill_attn_impl(q, q_token_stride, total_q, num_heads, k_cache, v_cache, k_row_stride, v_row_stride,
+                           num_slots, num_kv_heads, head_dim, block_tables, block_table_stride, block_size, plan_dev,
+                           plan_host, softmax_scale, out, out_token_stride, workspace, workspace_bytes, nullptr,
+                           nullptr, 0, 0, 0, stream);
+}
+
+extern "C" int vlc_prefill_attn_inflight(const void* q, int64_t q_token_stride, int total_q, int num_heads,
+                                         const void* k_cache, const void* v_cache, int64_t k_row_stride,
+                                         int64_t v_row_stride, int64_t num_slots, int num_kv_heads, int head_dim,
+                                         const int32_t* block_tables, int block_table_stride, int block_size,
+                                         const int32_t* plan_dev, const int32_t* plan_host, float softmax_scale,
+                                         void* out, int64_t out_token_stride, void* workspace,
+                                         int64_t workspace_bytes, const void* k_new, const void* v_new,
+                                         int64_t kn_row_stride, int64_t vn_row_stride, int64_t num_new_rows,
+                                         void* stream) {
+  if (!k_new || !v_new) return VLC_ERR_NULL;
+  return prefill_attn_impl(q, q_token_stride, total_q, num_heads, k_cache, v_cache, k_row_stride, v_row_stride,
+                           num_slots, num_kv_heads, head_dim, block_tables, block_table_stride, block_size, plan_dev,
+                           plan_host, softmax_scale, out, out_token_stride, workspace, workspace_bytes, k_new, v_new,
+                           kn_row_stride, vn_row_stride, num_new_rows, stream);
 }

@@ -94,14 +94,20 @@ class Attention(nn.Module):
                 have_cache = False  # stored
             else:                   # cold prefill reads the in-flight K: rotate it too
                 q, k = rotary_emb(positions, q, k)
+        stored_plain = False  # k / v hold exactly the rows store_kvcache copied into the cache
         if have_cache:
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+            stored_plain = True
         if context.is_prefill:
             plan = _prefill_plan(context, self.num_heads, self.num_kv_heads, q.device)
             ws = _workspace(context, plan.workspace_bytes, q.device)
             if context.block_tables is not None:    # prefix cache / warm request: paged K/V
+                # k / v (when given) are the rows just stored: self-attention sequences read
+                # them directly and do not wait for the scatter
+                inflight = k is not None and stored_plain
                 o = ops.prefill_attention(q, k_cache, v_cache, context.block_tables, plan, self.scale,
-                                          workspace=ws)
+                                          workspace=ws, k_new=k if inflight else None,
+                                          v_new=v if inflight else None)
             else:                                   # cold prefill: the in-flight K/V
                 o = ops.prefill_attention(q, k, v, None, plan, self.scale, workspace=ws)
         else:    # decode

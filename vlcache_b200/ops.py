@@ -235,7 +235,8 @@ def build_prefill_plan(cu_seqlens_q, cu_seqlens_k, num_heads: int, num_kv_heads:
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_tables: torch.Tensor | None,
                       plan: PrefillPlan, softmax_scale: float, out: torch.Tensor | None = None,
-                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+                      workspace: torch.Tensor | None = None, k_new: torch.Tensor | None = None,
+                      v_new: torch.Tensor | None = None) -> torch.Tensor:
     """Causal (bottom-right) varlen attention — the flash_attn_varlen_func contract.
 
     Paged: ``k``/``v`` are one layer's ``[num_blocks, block_size, Hk, D]`` caches and
@@ -243,6 +244,11 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_t
     are ``[total_k, Hk, D]`` (any token stride) laid out by cu_seqlens_k.
     The kernel is a programmatic dependent launch of the previous kernel on the
     stream: that kernel may produce q/k/v, but not the plan or ``block_tables``.
+
+    Paged with ``k_new``/``v_new`` (the step's in-flight ``[total_q, Hk, D]`` rows, row i
+    for query row i): sequences with q_len == k_len read their keys from those rows and
+    start without waiting for the previous kernel, which may then only write the cache
+    (the KV scatter, an ordinary launch) — ``vlc_prefill_attn_inflight``.
     """
     _require_cuda(q, k, v, block_tables)
     assert q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
@@ -271,6 +277,19 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_t
                                      < plan.workspace_bytes):
         workspace = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    if k_new is not None:
+        assert block_tables is not None and v_new is not None, "in-flight K/V go with a paged cache"
+        _require_cuda(k_new, v_new)
+        assert k_new.dim() == 3 and v_new.dim() == 3 and k_new.shape[1:] == (Hk, hd) and v_new.shape[1:] == (Hk, hd)
+        assert k_new.shape[0] == v_new.shape[0] >= total_q
+        assert k_new.stride(-1) == 1 and k_new.stride(-2) == hd and v_new.stride(-1) == 1 and v_new.stride(-2) == hd
+        st = lib().vlc_prefill_attn_inflight(_ptr(q), q.stride(0), total_q, H, _ptr(k), _ptr(v), k_stride, v_stride,
+                                             rows, Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev),
+                                             plan.host.ctypes.data, float(softmax_scale), _ptr(out), out.stride(0),
+                                             _ptr(workspace), ws_bytes, _ptr(k_new), _ptr(v_new), k_new.stride(0),
+                                             v_new.stride(0), k_new.shape[0], _stream())
+        check("vlc_prefill_attn_inflight", st)
+        return out
     st = lib().vlc_prefill_attn(_ptr(q), q.stride(0), total_q, H, _ptr(k), _ptr(v), k_stride, v_stride, rows,
                                 Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev), plan.host.ctypes.data,
                                 float(softmax_scale), _ptr(out), out.stride(0), _ptr(workspace), ws_bytes,
