@@ -123,7 +123,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
 }
 
 // 1-D bulk copy global -> this CTA's shared memory (16-byte aligned addresses, size a
-// multiple of 16), completion counted on `bar`; no multicast.
+// multiple of 16), completion counted on `bar`; the data lands in this CTA only.
 __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
@@ -284,7 +284,7 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // 2-D TMA load into this CTA's shared memory whose completion is counted on an mbarrier
-// of either CTA of the pair (here: the leader's); no multicast.
+// of either CTA of the pair (here: the leader's); the data lands in this CTA only.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar_cluster_addr, int x,
                                                  int y) {
   asm volatile(
@@ -315,14 +315,16 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint32_t a_lo, uin
       "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %5, p;\n\t}" ::"r"(d_tmem),
       "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
 }
-// Arrive once on the mbarrier at `bar`'s offset in every CTA of `cta_mask` when the
-// pair's previously issued tcgen05 operations complete.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
+// Arrive once on the mbarrier at `bar`'s offset in both CTAs of the pair when the pair's
+// previously issued tcgen05 operations complete: one commit per CTA, the peer's barrier
+// through its cluster address.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  const uint32_t local = smem_u32(bar);
+  const uint32_t peer = mapa_shared(local, cluster_ctarank() ^ 1u);
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(local)
+               : "memory");
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- UMMA descriptors

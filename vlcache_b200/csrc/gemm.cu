@@ -555,7 +555,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
 //   * both CTAs' TMA loads complete on the leader's (rank 0) full barrier, which the leader's
 //     producer arms for both CTAs' bytes;
 //   * the leader issues 4 MMAs of 256 x 256 x 16 per K block and commits to the stage's empty
-//     barrier, and after a tile's last block to acc_full, in both CTAs (multicast commit);
+//     barrier, and after a tile's last block to acc_full, in both CTAs (a commit to each);
 //   * each CTA's epilogue reads its own 128 accumulator rows and arrives on the leader's
 //     acc_empty (256 arrivals) so the leader can reuse the TMEM half;
 //   * a cluster barrier after set-up (barriers initialised, TMEM allocated) and before
@@ -667,10 +667,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
           for (int k = 0; k < BK / 16; ++k)
             umma_ss_pair(d, a_lo + (uint32_t)(k * 2), hi, b_lo + (uint32_t)(k * 2), hi, IDESC_PAIR,
                          (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit_pair(empty + s, 0x3);
+          umma_commit_pair_both(empty + s);
         }
         if (!ok) break;
-        umma_commit_pair(acc_full + buf, 0x3);
+        umma_commit_pair_both(acc_full + buf);
       }
     }
   } else {
