@@ -149,6 +149,12 @@ int vlc_attention_plan(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
 int64_t vlc_attention_plan_capacity(const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int num_seqs,
                                     int num_heads, int num_kv_heads, int causal, int num_sms);
 
+/* Unit kind of the prefill plans built from now on (process-wide): 1 = pairs of query
+ * tiles sharing each K/V block on one SM; 2 = quads of tiles on CTA pairs (clusters of 2,
+ * tcgen05.mma.cta_group::2; each SM loads half of every K/V block); 0 = the default (1).
+ * Packed plans always use pairs.  A plan records its kind; vlc_prefill_attn follows it. */
+int vlc_prefill_set_kernel(int mode);
+
 /* Workspace bytes vlc_prefill_attn needs for a given (host) plan. */
 int64_t vlc_prefill_workspace_size(const int32_t* plan_host);
 

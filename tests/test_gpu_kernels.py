@@ -242,6 +242,34 @@ def test_prefill_inflight_kv(ops):
     assert torch.equal(out, ref)
 
 
+@pytest.mark.parametrize("num_sms", [148, 16])
+def test_prefill_quad_units(ops, num_sms):
+    """Quad units on CTA pairs (``PREFILL_QUADS``: clusters of 2, tcgen05.mma.cta_group::2,
+    each CTA loading half of every K/V block, ghost tiles in short quads; with 16 SMs the
+    long tiles split): against the oracle, and against the pairs kernel on the same inputs."""
+    H, Hk = 16, 2
+    case = make_warm_case([(16, 1024, 32, 102), (5, 300, 17, 30), (0, 200, 9, 1), (20, 4000, 48, 400)], H, Hk,
+                          device="cuda", seed=23)
+    outs = []
+    for mode in (ops.PREFILL_PAIRS, ops.PREFILL_QUADS):
+        ops.set_prefill_kernel(mode)
+        try:
+            plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, Hk, device="cuda", num_sms=num_sms)
+        finally:
+            ops.set_prefill_kernel(ops.PREFILL_DEFAULT)
+        assert int(plan.host[21]) == (1 if mode == ops.PREFILL_QUADS else 0)
+        ws = torch.empty(max(1, plan.workspace_bytes), dtype=torch.uint8, device="cuda")
+        outs.append(ops.prefill_attention(case.q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale,
+                                          workspace=ws))
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    ref = oatt.prefill_attention(case.q.cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    mx, mean = attn_errors(outs[1], ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+    assert float((outs[0].float() - outs[1].float()).abs().max()) <= ATT_MAX
+
+
 def test_prefill_cfg2_full_size(ops):
     """BASELINE config 2 (3B, 4K image, 10% recompute): 1,123 query rows x 10,617 keys."""
     H, Hk = 16, 2

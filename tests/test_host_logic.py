@@ -283,3 +283,52 @@ def test_planner_packs_short_noncausal_sequences(H, Hk, lens):
     assert int(ops.build_prefill_plan(cu, cu, H, Hk, 128, num_sms=8, causal=True).host[20]) == 0
     longer = np.array([0, T + 1], np.int32)
     assert int(ops.build_prefill_plan(longer, longer, H, Hk, 128, num_sms=8, causal=False).host[20]) == 0
+
+
+@pytest.mark.parametrize("H,Hk", [(16, 2), (28, 4)])
+def test_planner_quads_cover_pairs_exactly_once(H, Hk):
+    """Quad plans (CTA pairs): unit i is records 2i (even CTA) and 2i + 1 (odd CTA), sharing
+    sequence, KV head and key ranges; real tiles cover every visible (query token, KV head,
+    key block) exactly once, ghost tiles (part -2) only stand in on the odd CTA; CTA ranges
+    index CTA pairs and the grid is even."""
+    from vlcache_b200 import ops
+    cu_q = [0, 118, 150, 150 + 300, 150 + 300 + 9, 150 + 300 + 9 + 33]
+    cu_k = [0, 118, 118 + 1072, 118 + 1072 + 300, 118 + 1072 + 300 + 509, 118 + 1072 + 300 + 509 + 4000]
+    ops.set_prefill_kernel(ops.PREFILL_QUADS)
+    try:
+        plan = ops.build_prefill_plan(cu_q, cu_k, H, Hk, num_sms=32)
+    finally:
+        ops.set_prefill_kernel(ops.PREFILL_DEFAULT)
+    h = plan.host
+    assert int(h[21]) == 1
+    grid, nrec = int(h[2]), int(h[3])
+    assert grid % 2 == 0 and nrec % 2 == 0 and grid <= 32
+    cta = h[int(h[12]):int(h[12]) + grid // 2 + 1]
+    assert cta[0] == 0 and cta[-1] == nrec // 2 and np.all(np.diff(cta) >= 0)
+    recs = h[int(h[13]):int(h[13]) + nrec * UNIT_INTS].reshape(nrec, UNIT_INTS)
+    G, T = H // Hk, 128 // (H // Hk)
+    need = {}
+    for b in range(len(cu_q) - 1):
+        ql, kl = cu_q[b + 1] - cu_q[b], cu_k[b + 1] - cu_k[b]
+        for g in range(Hk):
+            for t in range(ql):
+                for kb in range((kl - ql + t) // 128 + 1):
+                    need[(cu_q[b] + t, g, kb)] = 0
+    for i in range(nrec // 2):
+        ev, od = recs[2 * i], recs[2 * i + 1]
+        for f in (0, 1, 2, 3, 4, 5, 15):               # seq, head, key range, kv_len, base, B's end
+            assert ev[f] == od[f]
+        assert (ev[12] > 0) == (od[12] > 0)             # both CTAs have a tile B, or neither
+        assert ev[10] != -2 and ev[14] != -2            # ghosts only on the odd CTA
+        for r in (ev, od):
+            tiles = _unit_tiles(r)
+            for ti, (qb, qc, kp0, part, kb0, kb1) in enumerate(tiles):
+                if part == -2:
+                    continue
+                assert 1 <= qc <= T
+                for t in range(qc):
+                    for kb in range(kb0, kb1):
+                        key = (qb + t, int(r[1]), kb)
+                        if key in need:
+                            need[key] += 1
+    assert all(v == 1 for v in need.values())

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple] = {
     "vlc_attention_plan": (c_int, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_i64, c_vp]),
     "vlc_attention_plan_capacity": (c_i64, [c_vp, c_vp, c_int, c_int, c_int, c_int, c_int]),
     "vlc_prefill_workspace_size": (c_i64, [c_vp]),
+    "vlc_prefill_set_kernel": (c_int, [c_int]),
     "vlc_prefill_attn": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int,
                                  c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_i64, c_vp, c_i64, c_vp]),
     "vlc_prefill_attn_inflight": (c_int, [c_vp, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_i64, c_i64, c_int, c_int,

@@ -293,6 +293,14 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, ui
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, uint32_t bar_cluster_addr, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
@@ -314,6 +322,16 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint32_t a_lo, uin
       "mov.b64 b, {%3, %4};\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], a, b, %5, p;\n\t}" ::"r"(d_tmem),
       "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
+}
+// D[tmem of both CTAs] (+)= A[tmem of both CTAs] * B[smem, both CTAs], issued by the leader.
+__device__ __forceinline__ void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 b, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], b, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate));
 }
 // Arrive once on the mbarrier at `bar`'s offset in both CTAs of the pair when the pair's
 // previously issued tcgen05 operations complete: one commit per CTA, the peer's barrier

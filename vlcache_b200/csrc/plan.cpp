@@ -14,6 +14,7 @@
 // falls back to 148 without a device): usable without a GPU.
 #include <algorithm>
 #include <array>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <queue>
@@ -124,7 +125,17 @@ void build_packed_tiles(const int32_t* cu_q, int num_seqs, int num_kv_heads, int
   }
 }
 
+// Unit kind of new plans: 0 / 1 pairs of tiles (prefill_attn_kernel), 2 quads of tiles
+// on CTA pairs (prefill_attn_quad_kernel; packed plans always use pairs).
+std::atomic<int> g_prefill_kernel{0};
+
 }  // namespace
+
+extern "C" int vlc_prefill_set_kernel(int mode) {
+  if (mode < 0 || mode > 2) return VLC_ERR_SHAPE;
+  g_prefill_kernel.store(mode);
+  return VLC_OK;
+}
 
 extern "C" int64_t vlc_attention_plan_capacity(const int32_t* cu_q, const int32_t* cu_k, int num_seqs,
                                                int num_heads, int num_kv_heads, int causal, int num_sms) {
@@ -141,7 +152,7 @@ extern "C" int64_t vlc_attention_plan_capacity(const int32_t* cu_q, const int32_
   int64_t total_kb = 0;
   for (const Tile& t : tiles) total_kb += t.n_kb;
   const int64_t max_units = (int64_t)tiles.size() + total_kb;
-  return vlc::kPlanHeaderInts + (num_sms + 1) + max_units * vlc::kUnitInts +
+  return vlc::kPlanHeaderInts + (num_sms + 1) + 2 * max_units * vlc::kUnitInts +
          (int64_t)tiles.size() * (vlc::kMergeInts + kTileRows) + (packed ? 2LL * cu_q[num_seqs] : 0);
 }
 
@@ -173,9 +184,24 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   struct Pair {
     int a, b;  // tile indices, b = -1 for a single tile
   };
-  std::vector<Pair> pairs;
+  // Quad mode: per (sequence, KV head), from the end, tiles (a0, a1, b0, b1) = (last, last - 1,
+  // last - 2, last - 3); the even CTA of a pair takes a0 and b0, the odd one a1 and b1, and the
+  // pair's MMAs run over a0's (and b0's) key blocks.  `pairs` then holds (a0, b0), `odd` (a1, b1).
+  const bool quad = g_prefill_kernel.load() == 2 && !packed;
+  const int bins = quad ? std::max(1, num_sms / 2) : num_sms;
+  std::vector<Pair> pairs, odd;
   pairs.reserve(tiles.size());
-  for (size_t i = 0; i < tiles.size();) {
+  for (size_t i = 0; quad && i < tiles.size();) {
+    size_t e = i;
+    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head) ++e;
+    for (int last = (int)e - 1; last >= (int)i; last -= 4) {
+      auto at = [&](int k) { return last - k >= (int)i ? last - k : -1; };
+      pairs.push_back(Pair{at(0), at(2)});
+      odd.push_back(Pair{at(1), at(3)});
+    }
+    i = e;
+  }
+  for (size_t i = 0; !quad && i < tiles.size();) {
     size_t e = i;
     while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head &&
            tiles[i].seq >= 0)  // packed tiles have keys of their own: never paired
@@ -221,10 +247,10 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   };
   // Longest-processing-time-first makespan of a set of unit costs on num_sms CTAs.
   auto lpt_makespan = [&](std::vector<double>& costs) {
-    if ((int)costs.size() <= num_sms) return costs.empty() ? 0.0 : *std::max_element(costs.begin(), costs.end());
+    if ((int)costs.size() <= bins) return costs.empty() ? 0.0 : *std::max_element(costs.begin(), costs.end());
     std::sort(costs.begin(), costs.end(), std::greater<double>());
     std::priority_queue<double, std::vector<double>, std::greater<double>> heap;
-    for (int c = 0; c < num_sms; ++c) heap.push(0.0);
+    for (int c = 0; c < bins; ++c) heap.push(0.0);
     double mk = 0.0;
     for (double c : costs) {
       const double l = heap.top() + c;
@@ -246,7 +272,7 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   }
   double best_M = max_pair;
   const double m_min = kUnitOverhead + kPartOverhead + 1.0 + kPairStep;  // a one-block part
-  if (total_unsplit / std::max(1, num_sms) < max_pair) {
+  if (total_unsplit / std::max(1, bins) < max_pair) {
     // Mean CTA load after splitting every pair to M (decreasing in M).
     auto mean_load = [&](double M) {
       double tot = 0.0;
@@ -255,7 +281,7 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
         const int nb_full = pr.b >= 0 ? tiles[pr.b].n_kb : 0;
         tot += tiles[pr.a].n_kb + kPairStep * nb_full + np * kUnitOverhead + (np > 1 ? np * kPartOverhead : 0.0);
       }
-      return tot / std::max(1, num_sms);
+      return tot / std::max(1, bins);
     };
     // M* where the largest unit meets the mean load, then the packed makespan
     // (LPT) of targets around it decides.
@@ -307,7 +333,9 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
     m[kMRows] = t.q_count * G;
     merges.push_back(m);
   };
-  for (const Pair& pr : pairs) {
+  std::vector<UnitRec> units_odd;  // quad mode: the odd CTA's record of each unit
+  for (size_t pi = 0; pi < pairs.size(); ++pi) {
+    const Pair& pr = pairs[pi];
     const Tile& ta = tiles[pr.a];
     const int n = ta.n_kb;
     const int np = parts_for(pr, best_M);
@@ -325,6 +353,19 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
     const int part_b = np_b > 1 ? num_parts : -1;
     if (np_b > 1) {
       add_merge(tiles[pr.b], part_b, np_b);
+      num_parts += np_b;
+    }
+    // The odd CTA's tiles (quad mode), each split like its even sibling; a missing one is
+    // a ghost of the sibling (runs, writes nothing).
+    const Pair po = quad ? odd[pi] : Pair{-1, -1};
+    const int part_a1 = quad && po.a >= 0 && np > 1 ? num_parts : -1;
+    if (part_a1 >= 0) {
+      add_merge(tiles[po.a], part_a1, np);
+      num_parts += np;
+    }
+    const int part_b1 = quad && po.b >= 0 && np_b > 1 ? num_parts : -1;
+    if (part_b1 >= 0) {
+      add_merge(tiles[po.b], part_b1, np_b);
       num_parts += np_b;
     }
     for (int i = 0; i < np; ++i) {
@@ -354,11 +395,35 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
       u.cost = pair_cost(i < np_b ? pr : Pair{pr.a, -1}, kb0, kb1) + (np > 1 ? kPartOverhead : 0.0);
       u.f[kUCost] = (int32_t)(u.cost * 16);
       units.push_back(u);
+      if (quad) {
+        UnitRec w = u;  // same key range, sequence and KV head
+        if (po.a >= 0) {
+          const Tile& t1 = tiles[po.a];
+          w.f[kUQBeginA] = t1.q_begin;
+          w.f[kUQCountA] = t1.q_count;
+          w.f[kUKpos0A] = t1.kpos0;
+          w.f[kUPartA] = part_a1 >= 0 ? part_a1 + i : -1;
+        } else {
+          w.f[kUPartA] = kGhostPart;
+        }
+        if (i < np_b) {
+          if (po.b >= 0) {
+            const Tile& t1 = tiles[po.b];
+            w.f[kUQBeginB] = t1.q_begin;
+            w.f[kUQCountB] = t1.q_count;
+            w.f[kUKpos0B] = t1.kpos0;
+            w.f[kUPartB] = part_b1 >= 0 ? part_b1 + i : -1;
+          } else {
+            w.f[kUPartB] = kGhostPart;
+          }
+        }
+        units_odd.push_back(w);
+      }
     }
   }
 
   const int num_units = (int)units.size();
-  const int grid = std::min(num_sms, num_units);
+  const int grid = std::min(bins, num_units);  // CTAs, or CTA pairs in quad mode
   // Longest-processing-time-first bin packing onto `grid` persistent CTAs (ties in
   // unit order); each CTA runs its units longest first.
   std::vector<std::pair<double, int>> order(num_units);
@@ -391,9 +456,10 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
     for (const auto& o : order) by_cta[fill[cta_of[o.second]]++] = o.second;
   }
 
+  const int recs = quad ? 2 : 1;  // records per unit (quad: the even and the odd CTA's)
   const int64_t off_cta = kPlanHeaderInts;
   const int64_t off_units = off_cta + grid + 1;
-  const int64_t off_merges = off_units + (int64_t)num_units * kUnitInts;
+  const int64_t off_merges = off_units + (int64_t)num_units * recs * kUnitInts;
   // Merge launch: 8 warps per block, kMRowsPerWarp rows per warp.
   std::vector<int32_t> merge_blocks;
   for (size_t i = 0; i < merges.size(); ++i) {
@@ -409,8 +475,8 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   for (int i = 0; i < kPlanHeaderInts; ++i) h[i] = 0;
   h[kPMagic] = kPlanMagic;
   h[kPVersion] = kPlanVersion;
-  h[kPGrid] = grid;
-  h[kPNumUnits] = num_units;
+  h[kPGrid] = grid * recs;
+  h[kPNumUnits] = num_units * recs;
   h[kPNumParts] = num_parts;
   h[kPNumMerges] = (int32_t)merges.size();
   h[kPRowsPerTile] = T * G;
@@ -428,6 +494,7 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   h[kPCausal] = causal != 0 ? 1 : 0;
   h[kPHeadDim] = head_dim;
   h[kPOffSegments] = (int32_t)off_segments;
+  h[kPQuad] = quad ? 1 : 0;
   if (packed) {
     int32_t* seg = h + off_segments;
     for (int b = 0; b < num_seqs; ++b)
@@ -441,7 +508,11 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   for (int c = 0; c <= grid; ++c) cta[c] = cta_begin[c];
   for (int pos = 0; pos < num_units; ++pos) {
     const UnitRec& u = units[by_cta[pos]];
-    for (int k = 0; k < kUnitInts; ++k) up[(int64_t)pos * kUnitInts + k] = u.f[k];
+    for (int k = 0; k < kUnitInts; ++k) up[((int64_t)pos * recs) * kUnitInts + k] = u.f[k];
+    if (quad) {
+      const UnitRec& w = units_odd[by_cta[pos]];
+      for (int k = 0; k < kUnitInts; ++k) up[((int64_t)pos * recs + 1) * kUnitInts + k] = w.f[k];
+    }
   }
   int32_t* mp = h + off_merges;
   for (size_t i = 0; i < merges.size(); ++i)

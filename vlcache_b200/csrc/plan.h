@@ -35,6 +35,8 @@ enum : int {
   kPHeadDim = 19,         // head_dim the plan was made for (64 < d <= 128, d % 16 == 0)
   kPOffSegments = 20,     // 0, or int32[total_q][2]: {first, end} token of each query token's
                           // sequence, for packed tiles (several short sequences in one tile)
+  kPQuad = 21,            // 1: quad units on CTA pairs (prefill_attn_quad_kernel): the CTA
+                          // ranges index CTA pairs, and unit i is records 2i (even CTA), 2i + 1
 };
 
 // A unit is one or two query tiles of one (sequence, KV head) over one range of
@@ -68,6 +70,9 @@ enum : int {
                    // first token in q, which is also its first key row in the in-flight K/V
                    // (the projection's output); -1 otherwise
 };
+
+// kUPartA / kUPartB of a ghost tile: a quad's stand-in for a missing tile (computed, not written)
+constexpr int kGhostPart = -2;
 
 // merge fields (one record per split query tile)
 constexpr int kMergeInts = 8;

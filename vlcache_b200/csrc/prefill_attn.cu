@@ -112,6 +112,9 @@ struct Params {
   CUtensorMap tm_kn;
   CUtensorMap tm_vn;
   int inflight;
+  // Quad kernel: the same K tensors with a box of 64 keys (a CTA's half of a block).
+  CUtensorMap tm_k64;
+  CUtensorMap tm_kn64;
 };
 
 struct Bars {
@@ -756,6 +759,612 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
   }
 }
 
+
+namespace quad {
+constexpr int KHALF_BYTES = 64 * 128;  // 64 keys x 64 dims (bf16): one dim-half of a CTA's K rows
+// v_landed barriers after prefill_attn_kernel's barriers (the odd CTA's)
+constexpr int QD_OFF_VL = OFF_BAR + NUM_BARS * 8;
+constexpr int QD_OFF_MISC = QD_OFF_VL + STAGES * 8;
+constexpr int QD_SMEM_BYTES = QD_OFF_MISC + 16 + 1024;
+static_assert(QD_SMEM_BYTES <= 232448, "shared memory budget");
+constexpr uint32_t IDESC_QK2 = umma_idesc_bf16(256, 128, false, false);
+constexpr uint32_t IDESC_PV2 = umma_idesc_bf16(256, 128, false, true);
+}  // namespace quad
+
+// tcgen05 commit to the same barrier in both CTAs of the pair (one commit each).
+__device__ __forceinline__ void commit_both(uint64_t* bar) { umma_commit_pair_both(bar); }
+
+// S = Q K^T on the pair: A = this CTA's 128 Q rows (two 64-dim halves of 16 KB), B = this CTA's
+// 64 K rows (two 64-dim halves of 8 KB); M = 256, N = 128.
+__device__ __forceinline__ void issue_qk_quad(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
+#pragma unroll
+  for (int k = 0; k < HD / 16; ++k) {
+    const uint32_t qa = (uint32_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
+    const uint32_t kb = (uint32_t)(((k >> 2) * quad::KHALF_BYTES + (k & 3) * 32) >> 4);
+    umma_ss_pair(d_tmem, q_lo + qa, DESC_HI, k_lo + kb, DESC_HI, quad::IDESC_QK2, k > 0 ? 1u : 0u);
+  }
+}
+
+// O += P V on the pair over keys [64 half, 64 half + 64): A = P from each CTA's TMEM, B = this
+// CTA's 64 dims of the V block (MN-major, one 128-row half).
+__device__ __forceinline__ void issue_pv_half_quad(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_lo, int half,
+                                                   bool accumulate) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int kk = half * 4 + k;
+    umma_ts_pair(o_tmem, p_tmem + kk * 8, v_lo + (uint32_t)((kk * 2048) >> 4), DESC_HI, quad::IDESC_PV2,
+                 (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+// Quad units on CTA pairs (clusters of 2, tcgen05.mma.cta_group::2).  A quad is four query
+// tiles of one (sequence, KV head) over one key range: tiles A0, B0 in the pair's even CTA
+// (rank 0, the leader) and A1, B1 in the odd one, with the same roles, TMEM layout and
+// softmax as prefill_attn_kernel.  The leader issues every MMA of the pair: S_X = Q_X K^T
+// with M = 256 (each CTA's own 128 Q rows; each CTA holds half of the K block, keys
+// [64 r, 64 r + 64)) and O_X += P_X V (P from each CTA's TMEM; each CTA holds half of the
+// V block, dims [64 r, 64 r + 64)).  Per SM, K/V loads and Q K^T operand reads halve.
+//   * both CTAs' TMA loads complete on the leader's q_full / k_full / v_full, armed by the
+//     leader for both CTAs' bytes;
+//   * both CTAs' softmax warps arrive on the leader's p_lo / p_hi (256 arrivals);
+//   * the leader's MMAs signal s_full, o_done and the ring's empty barriers in both CTAs
+//     (one commit per CTA), and the leader's issuer tells the odd CTA that a V block has
+//     landed (v_landed: the odd CTA zeroes its rows past the sequence end);
+//   * cluster barriers after set-up and before exit.
+// A ghost tile (kUPart == kGhostPart) fills a quad short of four tiles: it runs like its
+// sibling but writes nothing.
+template <bool kPacked>
+__global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_quad_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const Bars bars = make_bars(smem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + quad::QD_OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + quad::QD_OFF_MISC + 4);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int u_begin = __ldg(p.cta_offsets + (blockIdx.x >> 1));
+  const int u_end = __ldg(p.cta_offsets + (blockIdx.x >> 1) + 1);
+  uint64_t* v_landed = reinterpret_cast<uint64_t*>(smem + quad::QD_OFF_VL);  // [STAGES], odd CTA
+  auto unit_rec = [&](int ui) { return p.units + (2 * (int64_t)ui + rank) * kUnitInts; };
+
+  if (warp == 9) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int b = 0; b < QSLOTS; ++b) {
+      mbar_init(bars.q_full + b, 1);
+      mbar_init(bars.q_empty + b, 1);
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bars.k_full + s, 1);
+      mbar_init(bars.k_empty + s, 1);
+      mbar_init(bars.v_full + s, 1);
+      mbar_init(bars.v_empty + s, 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bars.s_full + x, 1);
+      mbar_init(bars.p_lo + x, 2 * kTileThreads);  // both CTAs' rows (leader's barriers)
+      mbar_init(bars.p_hi + x, 2 * kTileThreads);
+      mbar_init(bars.o_done + x, 1);
+    }
+    for (int s = 0; s < STAGES; ++s) mbar_init(v_landed + s, 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x == 0) pdl_launch_dependents();  // the merge may be scheduled as SMs free up
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+    if (p.inflight) {
+      tma_prefetch_desc(&p.tm_kn);
+      tma_prefetch_desc(&p.tm_vn);
+    }
+  }
+  if (warp == 10 && lane == 0) {
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_o128);
+    tma_prefetch_desc(&p.tm_p128);
+  }
+  // Rows beyond T*G of the Q slots are never written by TMA: zero them once so
+  // the unused accumulator rows stay finite.
+  for (int i = threadIdx.x; i < QSLOTS * BM; i += NUM_THREADS) {
+    const int r = i & 127;
+    if (r >= p.rows) {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      uint8_t* q = smem + OFF_Q + (i >> 7) * TILE_BYTES;
+      uint4* r0 = reinterpret_cast<uint4*>(q + r * 128);
+      uint4* r1 = reinterpret_cast<uint4*>(q + HALF_BYTES + r * 128);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        r0[k] = z;
+        r1[k] = z;
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before either uses the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 10) {
+    // ------------------------------------------------------------ Q producer
+    if (lane == 0) {
+      // The plan is never written by the kernel launched just before (only q/k/v
+      // are): the first unit's fields load while the wait runs.
+      int g = 0, ntile = 0, q_a = 0, q_b = 0;
+      auto fetch = [&](int ui) {
+        const int32_t* u = unit_rec(ui);
+        g = u[kUKvHead];
+        ntile = u[kUQCountB] > 0 ? 2 : 1;
+        q_a = u[kUQBeginA];
+        q_b = u[kUQBeginB];
+      };
+      if (u_begin < u_end) fetch(u_begin);
+      if (!p.inflight) pdl_wait();  // Q may be written by the preceding kernel
+      int load = 0;
+      for (int ui = u_begin; ui < u_end; ++ui) {
+        if (ui != u_begin) fetch(ui);
+        bool ok = true;
+        for (int x = 0; x < ntile; ++x, ++load) {
+          const int slot = load % QSLOTS;
+          if (load >= QSLOTS && !wait_or_abort(bars.q_empty + slot, (uint32_t)((load / QSLOTS) & 1) ^ 1u,
+                                               VLC_DEV_ERR_TIMEOUT + 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int q_begin = x == 0 ? q_a : q_b;
+          // At launch every CTA loads at once and HBM is the limit: the first tile's Q
+          // (an operand of the first Q K^T) lands before the second tile's is requested.
+          if (leader && load == 1 && !wait_or_abort(bars.q_full + 0, 0u, VLC_DEV_ERR_TIMEOUT + 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* qdst = smem + OFF_Q + slot * TILE_BYTES;
+          if (leader) mbar_expect_tx(bars.q_full + slot, 2 * 2 * p.rows * 128);  // both CTAs' bytes
+          const uint32_t qbar = mapa_shared(smem_u32(bars.q_full + slot), 0);
+          tma_load_3d_pair(qdst, &p.tm_q, qbar, 0, g * p.group, q_begin);
+          tma_load_3d_pair(qdst + HALF_BYTES, &p.tm_q, qbar, 64, g * p.group, q_begin);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ K/V producer
+    if (lane == 0) {
+      // Plan and block tables are never written by the kernel launched just before:
+      // the first unit's fields and its first page are read while the wait runs.
+      int g = 0, kb0 = 0, kb1 = 0, slot0 = 0;
+      bool infl = false;
+      const int32_t* u = nullptr;
+      auto fetch = [&](int ui) {
+        u = unit_rec(ui);
+        g = u[kUKvHead];
+        kb0 = u[kUKbBegin];
+        kb1 = u[kUKbEnd];
+        infl = unit_inflight(p, u);
+        slot0 = kb0 < kb1 ? key_block_slot(p, u, kb0) : 0;
+      };
+      if (u_begin < u_end) fetch(u_begin);
+      bool waited = false;  // K/V rows (paged or contiguous) may be written by the preceding kernel
+      int it = 0;
+      for (int ui = u_begin; ui < u_end; ++ui) {
+        if (ui != u_begin) fetch(ui);
+        if (!infl && !waited) {
+          pdl_wait();
+          waited = true;
+        }
+        const CUtensorMap* tk = infl ? &p.tm_kn64 : &p.tm_k64;  // box of 64 keys
+        const CUtensorMap* tv = infl ? &p.tm_vn : &p.tm_v;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          const int slot = kb == kb0 ? slot0 : key_block_slot(p, u, kb);
+          if (it >= STAGES && !wait_or_abort(bars.k_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 2, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // this CTA's keys [64 rank, 64 rank + 64): two 64-dim halves of 64 rows
+          uint8_t* kdst = smem + OFF_K + s * TILE_BYTES;
+          if (leader) mbar_expect_tx(bars.k_full + s, TILE_BYTES);  // both CTAs' halves
+          const uint32_t kbar = mapa_shared(smem_u32(bars.k_full + s), 0);
+          tma_load_3d_pair(kdst, tk, kbar, 0, g, slot + 64 * (int)rank);
+          tma_load_3d_pair(kdst + quad::KHALF_BYTES, tk, kbar, 64, g, slot + 64 * (int)rank);
+          if (it >= STAGES && !wait_or_abort(bars.v_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 3, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // Likewise the first K block lands before V and the next blocks are requested.
+          if (leader && it == 0 && !wait_or_abort(bars.k_full + 0, 0u, VLC_DEV_ERR_TIMEOUT + 3, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // this CTA's dims [64 rank, 64 rank + 64) of all 128 keys
+          uint8_t* vdst = smem + OFF_V + s * TILE_BYTES;
+          if (leader) mbar_expect_tx(bars.v_full + s, TILE_BYTES);  // both CTAs' halves
+          tma_load_3d_pair(vdst, tv, mapa_shared(smem_u32(bars.v_full + s), 0), 64 * (int)rank, g, slot);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    // Step j of a unit (K/V block kv = it + j): for tile A then tile B (while it has
+    // blocks): O += P(j) V(j), then S = Q K(j+1)^T.  At the unit's last step the
+    // next Q K^T is the next unit's block 0 (same K/V ring, next Q slots), so the
+    // softmax warps start the next unit while this one drains.
+    if (lane == 0 && leader && u_begin < u_end) {
+      const uint32_t q_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_Q), 16);
+      const uint32_t k_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_K), 16);
+      const uint32_t v_lo = umma_desc_sw128_lo(smem_u32(smem + OFF_V), HALF_BYTES);
+      constexpr uint32_t kTileLo = TILE_BYTES >> 4;  // one tile in descriptor address units
+      int qload = 0;  // Q loads consumed (slot = load % QSLOTS, same order as the Q producer)
+      struct Cur {
+        UnitView v;
+        int load_a, load_b;
+      };
+      auto next_unit = [&](int ui) {
+        Cur c;
+        c.v = unit_view(unit_rec(ui));
+        c.load_a = qload++;
+        c.load_b = c.v.n_b > 0 ? qload++ : -1;
+        return c;
+      };
+      auto wait_k = [&](int kv) {
+        return wait_or_abort(bars.k_full + kv % STAGES, (uint32_t)(kv / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 7,
+                             abort_flag);
+      };
+      // S_x = Q(load) K(kv)^T; `first`: the tile's first block (wait for its Q),
+      // `last`: its last block (release the Q slot once the MMA completes).
+      auto qk = [&](int x, int load, int kv, bool first, bool last) {
+        const int slot = load % QSLOTS;
+        if (first && !wait_or_abort(bars.q_full + slot, (uint32_t)(load / QSLOTS) & 1u, VLC_DEV_ERR_TIMEOUT + 6,
+                                    abort_flag))
+          return false;
+        tc_fence_after();
+        issue_qk_quad(tmem_base + TMEM_S + x * 128, q_lo + slot * kTileLo, k_lo + (kv % STAGES) * kTileLo);
+        commit_both(bars.s_full + x);
+        if (last) commit_both(bars.q_empty + slot);
+        return true;
+      };
+      Cur cur = next_unit(u_begin);
+      bool ok = wait_k(0) && qk(0, cur.load_a, 0, true, cur.v.n_a == 1) &&
+                (cur.v.n_b == 0 || qk(1, cur.load_b, 0, true, cur.v.n_b == 1));
+      if (ok) commit_both(bars.k_empty + 0);
+      int pv_a = 0, pv_b = 0;  // P*V issued per tile (p_lo / p_hi phases)
+      int it = 0;              // K/V block index of the current unit's block 0
+      for (int ui = u_begin; ok && ui < u_end; ++ui) {
+        const bool has_next = ui + 1 < u_end;
+        Cur nxt{};
+        if (has_next) nxt = next_unit(ui + 1);
+        for (int j = 0; j < cur.v.n_a; ++j) {
+          const int kv = it + j, s = kv % STAGES;
+          const bool last = j == cur.v.n_a - 1;
+          const bool more = !last || has_next;  // a block kv + 1 follows
+          // tile A
+          // V(kv) in both CTAs first: the odd CTA may zero rows of its half before its P
+          if (!wait_or_abort(bars.v_full + s, (uint32_t)(kv / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(mapa_shared(smem_u32(v_landed + s), 1));
+          if (!wait_or_abort(bars.p_lo + 0, (uint32_t)pv_a & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv_half_quad(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 0, j > 0);
+          if (!wait_or_abort(bars.p_hi + 0, (uint32_t)pv_a & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv_half_quad(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 1, true);
+          ++pv_a;
+          if (last) commit_both(bars.o_done + 0);
+          if (more && !wait_k(kv + 1)) {
+            ok = false;
+            break;
+          }
+          if (!last)
+            ok = qk(0, cur.load_a, kv + 1, false, j + 1 == cur.v.n_a - 1);
+          else if (has_next)
+            ok = qk(0, nxt.load_a, kv + 1, true, nxt.v.n_a == 1);
+          if (!ok) break;
+          // tile B
+          if (j < cur.v.n_b) {
+            if (!wait_or_abort(bars.p_lo + 1, (uint32_t)pv_b & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv_half_quad(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 0, j > 0);
+            if (!wait_or_abort(bars.p_hi + 1, (uint32_t)pv_b & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv_half_quad(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 1, true);
+            ++pv_b;
+            if (j == cur.v.n_b - 1)
+              commit_both(bars.o_done + 1);
+            else
+              ok = qk(1, cur.load_b, kv + 1, false, j + 1 == cur.v.n_b - 1);
+            if (!ok) break;
+          }
+          if (last && has_next && nxt.v.n_b > 0) {
+            ok = qk(1, nxt.load_b, kv + 1, true, nxt.v.n_b == 1);
+            if (!ok) break;
+          }
+          commit_both(bars.v_empty + s);
+          if (more) commit_both(bars.k_empty + (kv + 1) % STAGES);
+        }
+        it += cur.v.n_a;
+        cur = nxt;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (one warpgroup per tile)
+    const int x = warp >> 2;            // 0: tile A, 1: tile B
+    const int row = threadIdx.x & 127;  // == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem_base + lane_off + TMEM_S + x * 128;
+    const uint32_t o_addr = tmem_base + lane_off + TMEM_O + x * 128;
+    int t = 0;      // blocks of this tile processed (s_full / p_lo / p_hi phases)
+    int nunit = 0;  // units of this tile finished (o_done phases)
+    int qload = 0;  // Q loads of this CTA so far (the Q producer's order)
+    for (int ui = u_begin; ui < u_end; ++ui) {
+      const int32_t* u = unit_rec(ui);
+      const UnitView uv = unit_view(u);
+      const int n = x == 0 ? uv.n_a : uv.n_b;
+      const int my_load = qload + x;
+      qload += u[kUQCountB] > 0 ? 2 : 1;
+      if (n == 0) continue;
+      // The tile's Q slot is free for the epilogue when fewer than QSLOTS loads follow
+      // this tile's (no later Q lands in it).
+      int after = qload - 1 - my_load;
+      for (int uj = ui + 1; uj < u_end && after < QSLOTS; ++uj)
+        after += unit_rec(uj)[kUQCountB] > 0 ? 2 : 1;
+      const bool own_slot = after < QSLOTS;
+      const int g = u[kUKvHead];
+      const int kb0 = u[kUKbBegin];
+      const int kv_len = u[kUKvLen];
+      const int q_begin = u[x == 0 ? kUQBeginA : kUQBeginB];
+      const int q_count = u[x == 0 ? kUQCountA : kUQCountB];
+      const int kpos0 = u[x == 0 ? kUKpos0A : kUKpos0B];
+      const int part = u[x == 0 ? kUPartA : kUPartB];
+      const int tok = row / p.group;
+      const bool row_valid = row < p.rows && tok < q_count;
+      const int qpos = p.causal ? kpos0 + tok : kpos0;  // non-causal: kpos0 = k_len - 1
+
+      float m_use = -INFINITY;
+      float l_row = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n; ++j, ++t) {
+        if (!wait_or_abort(bars.s_full + x, (uint32_t)t & 1u, VLC_DEV_ERR_TIMEOUT + 9, abort_flag)) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        tc_fence_after();
+        const int key0 = (kb0 + j) * BN;
+        uint32_t sr[128];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld32(s_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[q * 32]));
+        tmem_wait_ld();
+        if (kPacked) {
+          // Packed tile (several short sequences, one key block = the same tokens): the row
+          // sees keys [lo, hi) of the block, its own sequence's; rows past q_count none.
+          int lo = 0, hi = 0;
+          if (row_valid) {
+            const int k_base = unit_rec(ui)[kUKBase];
+            lo = __ldg(p.segments + 2 * (int64_t)(q_begin + tok)) - k_base;
+            hi = __ldg(p.segments + 2 * (int64_t)(q_begin + tok) + 1) - k_base;
+          }
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c < lo || c >= hi) sr[c] = __float_as_uint(-INFINITY);
+        } else if (key0 + BN - 1 > kpos0) {  // block touches the causal diagonal
+          const int lim = qpos - key0;
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+        }
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = __uint_as_float(sr[k]);
+#pragma unroll
+        for (int c = 8; c < 128; c += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], __uint_as_float(sr[c + k]), __uint_as_float(sr[c + 8 + k]));
+        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) *
+                             p.scale_log2;
+        // Lazy rescaling: only move the reference max when it grows by > 2^8.
+        const bool need = m_tile > m_use + 8.0f;
+        const float m_new = need ? m_tile : m_use;
+        const float f = (need && m_use != -INFINITY) ? fast_exp2(m_use - m_new) : 1.0f;
+        m_use = m_new;
+        const float mref = (m_use == -INFINITY) ? 0.f : m_use;
+        // Keys past the sequence end: zero their V rows so 0 * garbage stays 0.  Tile A
+        // has every block of the unit, and its P*V runs first.
+        if (x == 0 && key0 + BN > kv_len) {
+          const int st = t % STAGES;
+          if (!wait_or_abort(leader ? bars.v_full + st : v_landed + st, (uint32_t)(t / STAGES) & 1u,
+                             VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (key0 + row >= kv_len) {
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            uint4* v0 = reinterpret_cast<uint4*>(smem + OFF_V + st * TILE_BYTES + row * 128);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v0[i] = z;
+          }
+          fence_proxy_async_smem();
+        }
+        // P = exp2(s * scale_log2 - mref) as bf16 pairs: key pair (2c, 2c+1) goes to S
+        // column c (its register is free: pair c reads registers 2c and 2c+1 >= c).  Each
+        // half of the keys is released to the MMA as soon as it is in TMEM.
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t negm2 = f2_pack(-mref, -mref);
+        uint64_t lsum = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int base = half * 64 + q * 32;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const uint64_t x2 =
+                  f2_fma(f2_pack(__uint_as_float(sr[base + 2 * c]), __uint_as_float(sr[base + 2 * c + 1])), scale2,
+                         negm2);
+              float x0, x1;
+              f2_unpack(x2, x0, x1);
+              const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+              lsum = f2_add(lsum, f2_pack(e0, e1));
+              sr[base + c] = pack_bf16x2(e0, e1);
+            }
+            tmem_st16(s_addr + (base >> 1), *reinterpret_cast<uint32_t(*)[16]>(&sr[base]));
+          }
+          if (half == 0 && __any_sync(0xffffffffu, f != 1.0f)) {
+            // O (stable: P(j-1) V(j-1) completed before S(j)) follows the moved max
+            // before this block's P V starts.
+#pragma unroll 1
+            for (int cb = 0; cb < 8; ++cb) {
+              uint32_t orr[16];
+              tmem_ld16(o_addr + cb * 16, orr);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 16; ++c) orr[c] = __float_as_uint(__uint_as_float(orr[c]) * f);
+              tmem_st16(o_addr + cb * 16, orr);
+            }
+            l_row *= f;
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          uint64_t* pb = half == 0 ? bars.p_lo + x : bars.p_hi + x;
+          if (leader)
+            mbar_arrive(pb);
+          else
+            mbar_arrive_cluster(mapa_shared(smem_u32(pb), 0));
+        }
+        {
+          float l0, l1;
+          f2_unpack(lsum, l0, l1);
+          l_row += l0 + l1;
+        }
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------- epilogue
+      if (!wait_or_abort(bars.o_done + x, (uint32_t)nunit & 1u, VLC_DEV_ERR_TIMEOUT + 12, abort_flag)) break;
+      ++nunit;
+      __syncwarp();
+      tc_fence_after();
+      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+      __nv_bfloat16* dst;
+      if (part < 0) {
+        const int head = g * p.group + (row - tok * p.group);
+        dst = p.out + (int64_t)(q_begin + tok) * p.out_token_stride + (int64_t)head * p.head_dim;
+      } else {
+        // Split partial: O / l as bf16 (the merge re-weights by l and the max).
+        dst = p.part_o + ((int64_t)part * BM + row) * HD;
+        reinterpret_cast<float2*>(p.part_ml)[(int64_t)part * BM + row] = make_float2(m_use, l_row);
+      }
+      const bool ghost = part == kGhostPart;
+      const bool store = ghost ? false : part < 0 ? row_valid : true;
+      uint32_t orr[128];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld32(o_addr + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[q * 32]));
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 64; ++c)
+        orr[c] = pack_bf16x2(__uint_as_float(orr[2 * c]) * inv, __uint_as_float(orr[2 * c + 1]) * inv);
+      if (!ghost && own_slot && (part >= 0 || q_count == p.tokens_per_tile)) {
+        // Full tile or split partial, Q slot free: the whole tile goes into the slot
+        // in the Q load's layout (128-byte swizzle: 16-byte chunk c of row r of a
+        // 64-column half at chunk c ^ (r % 8)) and leaves with two TMA stores.  The
+        // slot's last reader, this tile's final Q K^T, completed before o_done.
+        uint8_t* qs = smem + OFF_Q + (my_load % QSLOTS) * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          *reinterpret_cast<uint4*>(qs + (k >> 3) * HALF_BYTES + row * 128 + (((k & 7) ^ (row & 7)) << 4)) =
+              make_uint4(orr[4 * k], orr[4 * k + 1], orr[4 * k + 2], orr[4 * k + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1 + x, kTileThreads);
+        if (row == 0) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (part < 0) {
+              if (64 * h < p.head_dim)  // columns past head_dim are the zero padding
+                tma_store_3d(&p.tm_o128, qs + h * HALF_BYTES, 64 * h, g * p.group, q_begin);
+            } else {
+              tma_store_2d(&p.tm_p128, qs + h * HALF_BYTES, 64 * h, part * BM);
+            }
+          }
+          bulk_commit_group();
+        }
+      } else if (!ghost && (part >= 0 || q_count == p.tokens_per_tile)) {
+        // Full tile or split partial: stage 32 columns at a time in shared memory,
+        // alternating two buffers (64-byte swizzle: 16-byte chunk c of row r at chunk
+        // c ^ ((r / 2) % 4)), and let one thread write each with a TMA tensor store.
+        uint8_t* stg = smem + OFF_STG + x * STG_TILE;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          uint8_t* buf = stg + (r & 1) * STG_BUF;
+          if (row == 0) bulk_wait_read_allbut1();  // the store that used this buffer has read it
+          named_bar_sync(1 + x, kTileThreads);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(buf + row * 64 + ((c ^ ((row >> 1) & 3)) << 4)) =
+                make_uint4(orr[16 * r + 4 * c], orr[16 * r + 4 * c + 1], orr[16 * r + 4 * c + 2],
+                           orr[16 * r + 4 * c + 3]);
+          fence_proxy_async_smem();
+          named_bar_sync(1 + x, kTileThreads);
+          if (row == 0) {
+            if (part < 0) {
+              if (32 * r < p.head_dim) tma_store_3d(&p.tm_o, buf, 32 * r, g * p.group, q_begin);
+            } else {
+              tma_store_2d(&p.tm_p, buf, 32 * r, part * BM);
+            }
+            bulk_commit_group();
+          }
+        }
+      } else if (store) {
+        // Last, partial tile of a sequence: the tensor store would write the rows of
+        // the following tokens, so each valid row is written directly.
+        if (p.out_store32) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            if (c * 16 < p.head_dim)
+              st_global_v8(dst + c * 16, *reinterpret_cast<const uint32_t(*)[8]>(&orr[c * 8]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (c * 8 < p.head_dim)
+              *reinterpret_cast<uint4*>(dst + c * 8) =
+                  make_uint4(orr[4 * c], orr[4 * c + 1], orr[4 * c + 2], orr[4 * c + 3]);
+        }
+      }
+      tc_fence_before();
+    }
+    if (row == 0) bulk_wait_all();  // this tile's output stores are complete
+  }
+
+  __syncthreads();
+  cluster_sync();  // every remote arrival and every MMA into this CTA's TMEM is done
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+
 // Merge split units.  Part p holds O_p / l_p (bf16), its max m_p and sum l_p:
 //   O = sum_p w_p (O_p / l_p) / sum_p w_p,   w_p = 2^(m_p - M) l_p.
 // 256-thread blocks listed by the planner as (merge, first row).  A warp is 4
@@ -990,9 +1599,30 @@ static int prefill_attn_impl(const void* q, int64_t q_token_stride, int total_q,
   if (prm.segments != nullptr && block_tables != nullptr) return VLC_ERR_PLAN;  // packed tiles: contiguous K/V
 
   const bool packed = prm.segments != nullptr;
-  static std::atomic<uint64_t> smem_set{0}, smem_set_packed{0};
-  if (ensure_dynamic_smem(packed ? (const void*)prefill_attn_kernel<true> : (const void*)prefill_attn_kernel<false>,
-                          SMEM_BYTES, packed ? smem_set_packed : smem_set) != VLC_OK)
+  const bool quad_units = plan_host[kPQuad] != 0;
+  if (quad_units && (packed || grid % 2 != 0)) return VLC_ERR_PLAN;
+  if (quad_units) {
+    // the K tensors again with a box of 64 keys: each CTA of a pair loads half of a block
+    const uint64_t dims[3] = {(uint64_t)head_dim, (uint64_t)num_kv_heads, (uint64_t)num_slots};
+    const uint64_t ks[2] = {(uint64_t)head_dim * 2, (uint64_t)k_row_stride * 2};
+    const uint32_t box[3] = {64, 1, 64};
+    if (encode_tmap_bf16(&prm.tm_k64, k_cache, 3, dims, ks, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+    if (prm.inflight) {
+      const uint64_t dn[3] = {(uint64_t)head_dim, (uint64_t)num_kv_heads, (uint64_t)num_new_rows};
+      const uint64_t kns[2] = {(uint64_t)head_dim * 2, (uint64_t)kn_row_stride * 2};
+      if (encode_tmap_bf16(&prm.tm_kn64, k_new, 3, dn, kns, box, 128) != VLC_OK) return VLC_ERR_CUDA;
+    } else {
+      prm.tm_kn64 = prm.tm_k64;  // unused
+    }
+  } else {
+    prm.tm_k64 = prm.tm_k;  // unused
+    prm.tm_kn64 = prm.tm_k;
+  }
+  const void* kfn = quad_units ? (const void*)prefill_attn_quad_kernel<false>
+                               : (packed ? (const void*)prefill_attn_kernel<true> : (const void*)prefill_attn_kernel<false>);
+  const int smem_bytes = quad_units ? quad::QD_SMEM_BYTES : SMEM_BYTES;
+  static std::atomic<uint64_t> smem_set[3];
+  if (ensure_dynamic_smem(kfn, smem_bytes, smem_set[quad_units ? 2 : packed ? 1 : 0]) != VLC_OK)
     return VLC_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   // Both kernels are launched as programmatic dependents of their predecessor in the
@@ -1002,15 +1632,21 @@ static int prefill_attn_impl(const void* q, int64_t q_token_stride, int total_q,
   cudaLaunchAttribute pdl;
   pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   pdl.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attrs[2];
+  attrs[0] = pdl;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;  // quad units: clusters of 2 (CTA pairs)
+  attrs[1].val.clusterDim.x = 2;
+  attrs[1].val.clusterDim.y = 1;
+  attrs[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = st;
-  cfg.attrs = &pdl;
-  cfg.numAttrs = 1;
-  const cudaError_t le = packed ? cudaLaunchKernelEx(&cfg, prefill_attn_kernel<true>, prm)
-                                : cudaLaunchKernelEx(&cfg, prefill_attn_kernel<false>, prm);
+  cfg.attrs = attrs;
+  cfg.numAttrs = quad_units ? 2 : 1;
+  void* args[] = {&prm};
+  const cudaError_t le = cudaLaunchKernelExC(&cfg, kfn, args);
   if (le != cudaSuccess) {
     (void)cudaGetLastError();
     return VLC_ERR_CUDA;

@@ -205,6 +205,16 @@ class PrefillPlan:
         return [(int(r[0]), int(r[1]), int(r[2])) for r in rec]
 
 
+PREFILL_DEFAULT, PREFILL_PAIRS, PREFILL_QUADS = 0, 1, 2
+
+
+def set_prefill_kernel(mode: int) -> None:
+    """Unit kind of the prefill plans built from now on: ``PREFILL_PAIRS`` (two query tiles
+    per unit on one SM), ``PREFILL_QUADS`` (four tiles per unit on a CTA pair) or
+    ``PREFILL_DEFAULT``.  Each plan records its kind; the launch follows the plan."""
+    check("vlc_prefill_set_kernel", lib().vlc_prefill_set_kernel(int(mode)))
+
+
 def build_prefill_plan(cu_seqlens_q, cu_seqlens_k, num_heads: int, num_kv_heads: int, head_dim: int = HEAD_DIM,
                        num_sms: int = 0, device: torch.device | str | None = None, causal: bool = True) -> PrefillPlan:
     """Plan the warm-prefill attention launch from HOST cu_seqlens (lists/arrays/CPU tensors).
