@@ -258,7 +258,8 @@ def test_cache_budget_matches_reference_rule():
                                         (16, 2, [16, 3, 16, 9, 7, 16, 1])])
 def test_planner_packs_short_noncausal_sequences(H, Hk, lens):
     """Non-causal self-attention of sequences that fit a tile (vision windows) packs whole
-    consecutive sequences into single-block tiles; every token is in exactly one tile per
+    consecutive sequences into single-block tiles, two independent tiles of one KV head per
+    unit (each with the key block of its own rows); every token is in exactly one tile per
     KV head, and the plan's segment table gives each token its sequence's bounds."""
     from vlcache_b200 import ops
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
@@ -269,11 +270,15 @@ def test_planner_packs_short_noncausal_sequences(H, Hk, lens):
     seen = np.zeros((int(cu[-1]), Hk), np.int32)
     starts = set(cu[:-1].tolist())
     for u in units:
-        assert int(u[0]) == -1 and int(u[12]) == 0 and int(u[3]) - int(u[2]) == 1   # single, one block
+        assert int(u[0]) == -1 and int(u[3]) - int(u[2]) == 1                      # packed, one block
         q0, qc = int(u[7]), int(u[8])
         assert 0 < qc <= T and q0 in starts and (q0 + qc) in set(cu.tolist())   # whole sequences
-        assert int(u[4]) == qc and int(u[5]) == q0
+        assert int(u[4]) == qc and int(u[5]) == q0                               # tile A's keys: its rows
         seen[q0:q0 + qc, int(u[1])] += 1
+        if int(u[12]) > 0:                                                       # tile B: its own rows
+            qb, qcb = int(u[11]), int(u[12])
+            assert 0 < qcb <= T and qb in starts and (qb + qcb) in set(cu.tolist()) and int(u[15]) == 1
+            seen[qb:qb + qcb, int(u[1])] += 1
     assert np.all(seen == 1)
     off = int(plan.host[20])
     seg = plan.host[off:off + 2 * int(cu[-1])].reshape(-1, 2)

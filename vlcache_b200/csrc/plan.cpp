@@ -203,9 +203,8 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   }
   for (size_t i = 0; !quad && i < tiles.size();) {
     size_t e = i;
-    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head &&
-           tiles[i].seq >= 0)  // packed tiles have keys of their own: never paired
-      ++e;
+    // (packed tiles, all of sequence -1, pair by KV head: each keeps its own key block)
+    while (e < tiles.size() && tiles[e].seq == tiles[i].seq && tiles[e].kv_head == tiles[i].kv_head) ++e;
     if (e == i) e = i + 1;
     int last = (int)e - 1;
     while (last >= (int)i) {
@@ -223,7 +222,8 @@ extern "C" int vlc_attention_plan(const int32_t* cu_q, const int32_t* cu_k, int 
   // Time model, in single-tile key-block steps (measured on B200: a step of a
   // paired unit costs about 1.2 steps, each unit about 1.5 steps of start, drain and
   // epilogue; a split part adds a partial write and its share of the merge).
-  const double kUnitOverhead = 1.5, kPartOverhead = 0.1, kPairStep = 0.2;
+  const double kUnitOverhead = 1.5, kPartOverhead = 0.1;
+  const double kPairStep = packed ? 1.0 : 0.2;  // packed pairs share no K/V block
   auto pair_cost = [&](const Pair& pr, int kb0, int kb1) {
     const int nb = pr.b >= 0 ? std::max(0, std::min(kb1, tiles[pr.b].n_kb) - kb0) : 0;
     return (kb1 - kb0) + kPairStep * nb + kUnitOverhead;

@@ -367,10 +367,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         const CUtensorMap* tk = infl ? &p.tm_kn : &p.tm_k;
         const CUtensorMap* tv = infl ? &p.tm_vn : &p.tm_v;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        // A packed unit's tile B has a key block of its own (its rows), next in the ring.
+        const int kb_end = kPacked && u[kUQCountB] > 0 ? kb0 + 2 : kb1;
+        for (int kb = kb0; kb < kb_end; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          const int slot = kb == kb0 ? slot0 : key_block_slot(p, u, kb);
+          const int slot = kb == kb0 ? slot0 : kPacked ? u[kUQBeginB] : key_block_slot(p, u, kb);
           if (it >= STAGES && !wait_or_abort(bars.k_empty + s, ph ^ 1u, VLC_DEV_ERR_TIMEOUT + 2, abort_flag)) {
             ok = false;
             break;
@@ -436,9 +438,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         if (last) umma_commit(bars.q_empty + slot);
         return true;
       };
-      Cur cur = next_unit(u_begin);
-      bool ok = wait_k(0) && qk(0, cur.load_a, 0, true, cur.v.n_a == 1) &&
-                (cur.v.n_b == 0 || qk(1, cur.load_b, 0, true, cur.v.n_b == 1));
+      if constexpr (kPacked) {
+        // Packed units: tile A and tile B (when present) each have one key block of their
+        // own, ring blocks r and r + 1.  Order: S_A, S_B of the first unit; then per unit
+        // O_A += P_A V_A, the next unit's S_A, O_B += P_B V_B, the next unit's S_B.
+        struct PU {
+          bool has_b;
+          int load_a, load_b, ra, rb;
+        };
+        int r = 0, pv_a = 0, pv_b = 0;
+        auto fetch_pu = [&](int ui) {
+          PU c;
+          c.has_b = p.units[(int64_t)ui * kUnitInts + kUQCountB] > 0;
+          c.load_a = qload++;
+          c.load_b = c.has_b ? qload++ : -1;
+          c.ra = r++;
+          c.rb = c.has_b ? r++ : -1;
+          return c;
+        };
+        auto qk1 = [&](int x, int load, int rb) {  // a tile's only block: first and last
+          if (!wait_k(rb)) return false;
+          if (!qk(x, load, rb, true, true)) return false;
+          umma_commit(bars.k_empty + rb % STAGES);
+          return true;
+        };
+        auto pv1 = [&](int x, int rb, int& pvc) {
+          const int s = rb % STAGES;
+          if (!wait_or_abort(bars.v_full + s, (uint32_t)(rb / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 5, abort_flag) ||
+              !wait_or_abort(bars.p_lo + x, (uint32_t)pvc & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag))
+            return false;
+          tc_fence_after();
+          issue_pv_half(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 0, false);
+          if (!wait_or_abort(bars.p_hi + x, (uint32_t)pvc & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) return false;
+          tc_fence_after();
+          issue_pv_half(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 1, true);
+          ++pvc;
+          umma_commit(bars.o_done + x);
+          umma_commit(bars.v_empty + s);
+          return true;
+        };
+        PU pc = fetch_pu(u_begin);
+        bool pok = qk1(0, pc.load_a, pc.ra) && (!pc.has_b || qk1(1, pc.load_b, pc.rb));
+        for (int ui = u_begin; pok && ui < u_end; ++ui) {
+          const bool has_next = ui + 1 < u_end;
+          PU pn{};
+          if (has_next) pn = fetch_pu(ui + 1);
+          pok = pv1(0, pc.ra, pv_a) && (!has_next || qk1(0, pn.load_a, pn.ra));
+          if (pok && pc.has_b) pok = pv1(1, pc.rb, pv_b);
+          if (pok && has_next && pn.has_b) pok = qk1(1, pn.load_b, pn.rb);
+          pc = pn;
+        }
+      }
+      Cur cur{};
+      bool ok = !kPacked;
+      if (!kPacked) {
+        cur = next_unit(u_begin);
+        ok = wait_k(0) && qk(0, cur.load_a, 0, true, cur.v.n_a == 1) &&
+             (cur.v.n_b == 0 || qk(1, cur.load_b, 0, true, cur.v.n_b == 1));
+      }
       if (ok) umma_commit(bars.k_empty + 0);
       int pv_a = 0, pv_b = 0;  // P*V issued per tile (p_lo / p_hi phases)
       int it = 0;              // K/V block index of the current unit's block 0
@@ -516,6 +573,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
     const uint32_t o_addr = tmem_base + lane_off + TMEM_O + x * 128;
     int t = 0;      // blocks of this tile processed (s_full / p_lo / p_hi phases)
     int nunit = 0;  // units of this tile finished (o_done phases)
+    int ring = 0;   // K/V ring blocks of the CTA's earlier units
     int qload = 0;  // Q loads of this CTA so far (the Q producer's order)
     for (int ui = u_begin; ui < u_end; ++ui) {
       const int32_t* u = p.units + (int64_t)ui * kUnitInts;
@@ -523,6 +581,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       const int n = x == 0 ? uv.n_a : uv.n_b;
       const int my_load = qload + x;
       qload += u[kUQCountB] > 0 ? 2 : 1;
+      // packed: tile B's keys are its own rows, in the ring block after tile A's
+      const int ring0 = ring + (kPacked && x == 1 ? 1 : 0);
+      ring += kPacked ? (u[kUQCountB] > 0 ? 2 : 1) : uv.n_a;
       if (n == 0) continue;
       // The tile's Q slot is free for the epilogue when fewer than QSLOTS loads follow
       // this tile's (no later Q lands in it).
@@ -532,7 +593,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
       const bool own_slot = after < QSLOTS;
       const int g = u[kUKvHead];
       const int kb0 = u[kUKbBegin];
-      const int kv_len = u[kUKvLen];
+      const int kv_len = kPacked && x == 1 ? u[kUQCountB] : u[kUKvLen];
       const int q_begin = u[x == 0 ? kUQBeginA : kUQBeginB];
       const int q_count = u[x == 0 ? kUQCountA : kUQCountB];
       const int kpos0 = u[x == 0 ? kUKpos0A : kUKpos0B];
@@ -561,7 +622,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
           // sees keys [lo, hi) of the block, its own sequence's; rows past q_count none.
           int lo = 0, hi = 0;
           if (row_valid) {
-            const int k_base = p.units[(int64_t)ui * kUnitInts + kUKBase];
+            const int k_base = x == 1 ? u[kUQBeginB] : u[kUKBase];
             lo = __ldg(p.segments + 2 * (int64_t)(q_begin + tok)) - k_base;
             hi = __ldg(p.segments + 2 * (int64_t)(q_begin + tok) + 1) - k_base;
           }
@@ -591,9 +652,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
         const float mref = (m_use == -INFINITY) ? 0.f : m_use;
         // Keys past the sequence end: zero their V rows so 0 * garbage stays 0.  Tile A
         // has every block of the unit, and its P*V runs first.
-        if (x == 0 && key0 + BN > kv_len) {
-          const int st = t % STAGES;
-          if (!wait_or_abort(bars.v_full + st, (uint32_t)(t / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) {
+        if ((kPacked || x == 0) && key0 + BN > kv_len) {
+          const int rb = kPacked ? ring0 : t;  // ring index of this block (tile A's count = the ring's)
+          const int st = rb % STAGES;
+          if (!wait_or_abort(bars.v_full + st, (uint32_t)(rb / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 11, abort_flag)) {
             ok = false;
             break;
           }
