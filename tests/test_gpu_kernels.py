@@ -323,6 +323,48 @@ def test_prefill_long_keys_max_parts(ops):
     assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
 
 
+@pytest.mark.parametrize("num_sms", [148, 16])
+def test_prefill_split_back_to_back(ops, num_sms):
+    """Launches with split tiles on one plan and workspace run back to back (each attention a
+    programmatic dependent of the previous merge), eagerly and in a replayed graph, with
+    different queries each time: every output equals that of a launch of its own."""
+    H, Hk = 16, 2
+    case = make_warm_case([(20, 6000, 48, 300), (0, 900, 64, 0)], H, Hk, device="cuda", seed=29)
+    plan = ops.build_prefill_plan(case.cu_q, case.cu_k, H, Hk, device="cuda", num_sms=num_sms)
+    assert plan.num_merges > 0
+    ws = torch.empty(plan.workspace_bytes, dtype=torch.uint8, device="cuda")
+    qs = [case.q * s for s in (1.0, 0.5, -0.75, 1.25)]
+    solo = []
+    for q in qs:
+        o = torch.empty_like(q)
+        ops.prefill_attention(q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale, o, ws)
+        torch.cuda.synchronize()
+        solo.append(o)
+    outs = [torch.empty_like(q) for q in qs]
+    for q, o in zip(qs, outs):
+        ops.prefill_attention(q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale, o, ws)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for o, r in zip(outs, solo):
+        assert torch.equal(o, r)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for q, o in zip(qs, outs):
+            ops.prefill_attention(q, case.k_cache, case.v_cache, case.block_tables, plan, case.scale, o, ws)
+    for _ in range(3):
+        for o in outs:
+            o.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for o, r in zip(outs, solo):
+        assert torch.equal(o, r)
+    ref = oatt.prefill_attention(qs[2].cpu(), case.k_cache.cpu(), case.v_cache.cpu(), case.block_tables.cpu(),
+                                 case.cu_q, case.cu_k, case.scale)
+    mx, mean = attn_errors(outs[2], ref)
+    assert mx <= ATT_MAX and mean <= ATT_MEAN, (mx, mean)
+
+
 # ------------------------------------------------------------------ decode
 @pytest.mark.parametrize("model,lens", [("7b", [1, 63, 64, 65, 700, 2711, 5000, 10700]),
                                         ("3b", [255, 256, 257, 4097])])
