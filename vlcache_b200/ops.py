@@ -18,12 +18,21 @@ HEAD_DIM = 128
 DEFAULT_MROPE_SECTION = (16, 24, 24)  # Qwen2.5-VL rope_scaling.mrope_section
 
 
-def _stream() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+_raw_device = getattr(torch._C, "_cuda_getDevice", None)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
-    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+def _stream() -> int:
+    """Handle of the current device's current stream.  Read raw (no torch.cuda.Stream object,
+    no device-availability probe): it is on every launch's host path."""
+    if _raw_device is not None and _raw_stream is not None:
+        return _raw_stream(_raw_device())
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int:
+    """Device address of ``t`` (0 for None); every C-ABI argument is declared ``void*``."""
+    return 0 if t is None else t.data_ptr()
 
 
 def _require_cuda(*ts: torch.Tensor) -> None:
@@ -182,6 +191,14 @@ class PrefillPlan:
     workspace_bytes: int
 
     @property
+    def host_ptr(self) -> int:
+        """Address of ``host`` (cached: the launch path passes it on every call)."""
+        p = self.__dict__.get("_host_ptr")
+        if p is None:
+            p = self.__dict__["_host_ptr"] = int(self.host.ctypes.data)
+        return p
+
+    @property
     def grid(self) -> int:
         return int(self.host[2])
 
@@ -295,13 +312,13 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, block_t
         assert k_new.stride(-1) == 1 and k_new.stride(-2) == hd and v_new.stride(-1) == 1 and v_new.stride(-2) == hd
         st = lib().vlc_prefill_attn_inflight(_ptr(q), q.stride(0), total_q, H, _ptr(k), _ptr(v), k_stride, v_stride,
                                              rows, Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev),
-                                             plan.host.ctypes.data, float(softmax_scale), _ptr(out), out.stride(0),
+                                             plan.host_ptr, float(softmax_scale), _ptr(out), out.stride(0),
                                              _ptr(workspace), ws_bytes, _ptr(k_new), _ptr(v_new), k_new.stride(0),
                                              v_new.stride(0), k_new.shape[0], _stream())
         check("vlc_prefill_attn_inflight", st)
         return out
     st = lib().vlc_prefill_attn(_ptr(q), q.stride(0), total_q, H, _ptr(k), _ptr(v), k_stride, v_stride, rows,
-                                Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev), plan.host.ctypes.data,
+                                Hk, hd, bt_ptr, bt_stride, block_size, _ptr(plan.dev), plan.host_ptr,
                                 float(softmax_scale), _ptr(out), out.stride(0), _ptr(workspace), ws_bytes,
                                 _stream())
     check("vlc_prefill_attn", st)
