@@ -204,29 +204,38 @@ __device__ __forceinline__ int key_block_slot(const Params& p, const int32_t* u,
 // half, +16 KB to the second half; MN-major V: +2 KB per 16 keys).
 constexpr uint32_t DESC_HI = umma_desc_sw128_hi(1024);
 
+// kSteps: 16-column steps of the head dim that are multiplied (head dim 80: 5, the padding
+// columns skipped; otherwise all 8).
+template <int kSteps = HD / 16>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_lo, uint32_t k_lo) {
 #pragma unroll
-  for (int k = 0; k < HD / 16; ++k) {
+  for (int k = 0; k < kSteps; ++k) {
     const uint32_t off = (uint32_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
     umma_ss_w(d_tmem, q_lo + off, DESC_HI, k_lo + off, DESC_HI, IDESC_QK, k > 0 ? 1u : 0u);
   }
 }
 
-// O += P V over keys [64 half, 64 half + 64) of the block.
+// O += P V over keys [64 half, 64 half + 64) of the block; kIdesc sets N (the O columns
+// computed: 80 for head dim 80, else 128).
+template <uint32_t kIdesc = IDESC_PV>
 __device__ __forceinline__ void issue_pv_half(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_lo, int half,
                                               bool accumulate) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int kk = half * 4 + k;
-    umma_ts_w(o_tmem, p_tmem + kk * 8, v_lo + (uint32_t)((kk * 2048) >> 4), DESC_HI, IDESC_PV,
+    umma_ts_w(o_tmem, p_tmem + kk * 8, v_lo + (uint32_t)((kk * 2048) >> 4), DESC_HI, kIdesc,
               (accumulate || kk > 0) ? 1u : 0u);
   }
 }
 
 // kPacked: the plan packs several short sequences per tile (block-diagonal mask); a separate
-// instantiation, so the causal path's code is not touched by it.
-template <bool kPacked>
+// instantiation, so the causal path's code is not touched by it.  kDK: 16-column steps of
+// the head dim in the MMAs (5 for head dim 80: Q K^T over its 80 columns and P V with N =
+// 80, instead of the zero-padded 128; 8 otherwise).  O columns past 16 kDK are never
+// written (nor stored: the epilogue writes the head dim's columns only).
+template <bool kPacked, int kDK>
 __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __grid_constant__ Params p) {
+  constexpr uint32_t kIdescPV = umma_idesc_bf16(128, 16 * kDK, false, true);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Bars bars = make_bars(smem);
@@ -433,7 +442,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
                                     abort_flag))
           return false;
         tc_fence_after();
-        issue_qk(tmem_base + TMEM_S + x * 128, q_lo + slot * kTileLo, k_lo + (kv % STAGES) * kTileLo);
+        issue_qk<kDK>(tmem_base + TMEM_S + x * 128, q_lo + slot * kTileLo, k_lo + (kv % STAGES) * kTileLo);
         umma_commit(bars.s_full + x);
         if (last) umma_commit(bars.q_empty + slot);
         return true;
@@ -468,10 +477,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
               !wait_or_abort(bars.p_lo + x, (uint32_t)pvc & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag))
             return false;
           tc_fence_after();
-          issue_pv_half(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 0, false);
+          issue_pv_half<kIdescPV>(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 0, false);
           if (!wait_or_abort(bars.p_hi + x, (uint32_t)pvc & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) return false;
           tc_fence_after();
-          issue_pv_half(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 1, true);
+          issue_pv_half<kIdescPV>(tmem_base + TMEM_O + x * 128, tmem_base + TMEM_S + x * 128, v_lo + s * kTileLo, 1, true);
           ++pvc;
           umma_commit(bars.o_done + x);
           umma_commit(bars.v_empty + s);
@@ -514,13 +523,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
             break;
           }
           tc_fence_after();
-          issue_pv_half(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 0, j > 0);
+          issue_pv_half<kIdescPV>(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 0, j > 0);
           if (!wait_or_abort(bars.p_hi + 0, (uint32_t)pv_a & 1u, VLC_DEV_ERR_TIMEOUT + 4, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv_half(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 1, true);
+          issue_pv_half<kIdescPV>(tmem_base + TMEM_O, tmem_base + TMEM_S, v_lo + s * kTileLo, 1, true);
           ++pv_a;
           if (last) umma_commit(bars.o_done + 0);
           if (more && !wait_k(kv + 1)) {
@@ -539,13 +548,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) prefill_attn_kernel(const __gr
               break;
             }
             tc_fence_after();
-            issue_pv_half(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 0, j > 0);
+            issue_pv_half<kIdescPV>(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 0, j > 0);
             if (!wait_or_abort(bars.p_hi + 1, (uint32_t)pv_b & 1u, VLC_DEV_ERR_TIMEOUT + 8, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_pv_half(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 1, true);
+            issue_pv_half<kIdescPV>(tmem_base + TMEM_O + 128, tmem_base + TMEM_S + 128, v_lo + s * kTileLo, 1, true);
             ++pv_b;
             if (j == cur.v.n_b - 1)
               umma_commit(bars.o_done + 1);
@@ -1688,12 +1697,16 @@ static int prefill_attn_impl(const void* q, int64_t q_token_stride, int total_q,
     prm.tm_k64 = prm.tm_k;  // unused
     prm.tm_kn64 = prm.tm_k;
   }
+  // Head dim 80 (the vision tower's) multiplies its 80 columns only; other head dims run on
+  // the zero-padded 128 columns.
+  const bool d80 = head_dim == 80;
   const void* kfn = quad_units ? (const void*)prefill_attn_quad_kernel<false>
-                               : (packed ? (const void*)prefill_attn_kernel<true> : (const void*)prefill_attn_kernel<false>);
+                    : packed   ? (d80 ? (const void*)prefill_attn_kernel<true, 5> : (const void*)prefill_attn_kernel<true, 8>)
+                               : (d80 ? (const void*)prefill_attn_kernel<false, 5> : (const void*)prefill_attn_kernel<false, 8>);
   const int smem_bytes = quad_units ? quad::QD_SMEM_BYTES : SMEM_BYTES;
-  static std::atomic<uint64_t> smem_set[3];
-  if (ensure_dynamic_smem(kfn, smem_bytes, smem_set[quad_units ? 2 : packed ? 1 : 0]) != VLC_OK)
-    return VLC_ERR_CUDA;
+  static std::atomic<uint64_t> smem_set[5];
+  const int kind = quad_units ? 4 : (packed ? 1 : 0) + (d80 ? 2 : 0);
+  if (ensure_dynamic_smem(kfn, smem_bytes, smem_set[kind]) != VLC_OK) return VLC_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   // Both kernels are launched as programmatic dependents of their predecessor in the
   // stream (the attention: of the KV scatter; the merge: of the attention).  They wait
