@@ -333,11 +333,11 @@ def e2e_bench(wl: WarmPrefillWorkload, steps: int, warmup: int, dist_on: bool):
         meta_bytes[0] = (t["descriptors"].numel() + t["cu_seqlens_q"].numel() + t["cu_seqlens_k"].numel()) * 4 + \
             batch.plan.host.nbytes
         get_context().workspace = wl.ws
-        shift.shift_all_layers(wl.kv_cache, t["reuse_src"], t["reuse_dst"], wl.delta)
         # The uploads wait for the previous step's layers (which read the input buffers) and
-        # for this step's metadata and shift: starting them before the metadata and shift
-        # measured slower (5.9 vs 5.1 ms per step on one box).
+        # this step's metadata kernel, not for the shift that follows (measured on one box:
+        # 5.03-5.06 ms per step; after the shift 5.14-5.17; before the metadata 5.9).
         h2d.wait_stream(cur)
+        shift.shift_all_layers(wl.kv_cache, t["reuse_src"], t["reuse_dst"], wl.delta)
         with torch.cuda.stream(h2d):
             for l in range(LAYERS):
                 dev_qkv[l].copy_(host_qkv[l], non_blocking=True)
