@@ -305,10 +305,12 @@ int vlc_warm_metadata(const int32_t* vseq_desc, int num_vseqs, const int32_t* re
  * ------------------------------------------------------------------------ */
 int64_t vlc_linear_workspace_size(int kind, int m, int n, int k);
 
-/* Which GEMM kernel the linear entry points use, process-wide: 0 automatic (default),
- * 1 single-SM 128 x 256 tiles (with the stream-K split where it pays), 2 CTA pairs
- * (clusters of 2, tcgen05.mma.cta_group::2, 256 x 256 tiles).  A tuning and test switch;
- * results agree within the GEMM tolerance. */
+/* Which GEMM kernel the linear entry points use, process-wide: 0 automatic (default: a
+ * cost model fitted on B200 picks per shape), 1 single-SM 128 x 256 tiles (with the
+ * stream-K split where it pays), 2 CTA pairs (clusters of 2, tcgen05.mma.cta_group::2,
+ * 256 x 256 tiles), 3 single-SM 128 x 128 tiles, 4 single-SM 128 x 224 tiles (vlc_linear
+ * only; the fused epilogues use the automatic choice).  A tuning and test switch; results
+ * agree within the GEMM tolerance. */
 int vlc_linear_set_kernel(int mode);
 
 int vlc_linear(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias, void* out,

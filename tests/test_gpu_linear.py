@@ -20,9 +20,11 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[1, 2], ids=["single_sm", "cta_pair"])
+@pytest.fixture(params=[1, 2, 3, 4, 0], ids=["single_sm", "cta_pair", "single_sm_128", "single_sm_224", "auto"])
 def kernel_mode(request, cuda_lib):
-    """Run a test on the single-SM GEMM and on the CTA-pair (cta_group::2) GEMM."""
+    """Run a test on each GEMM configuration: single-SM 128 x 256 tiles, CTA pairs
+    (cta_group::2, 256 x 256), single-SM 128 x 128 and 128 x 224 (the plain epilogue; the
+    others fall back), and the automatic choice."""
     from vlcache_b200 import ops
     ops.set_linear_kernel(request.param)
     yield request.param

@@ -45,18 +45,26 @@ namespace vlc {
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
-constexpr int B_BYTES = BN * BK * 2;            // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
 constexpr int NUM_THREADS = 192;
-constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-constexpr int NUM_BARS = 2 * STAGES + 4;  // full[S], empty[S], acc_full[2], acc_empty[2]
-constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN, false, false);
+
+// Single-SM kernel with output tiles of BM x TN (TN = 256, or 224 / 128 where narrower
+// tiles fill the SMs of a short-M projection in one wave): as many stages of
+// A (16 KB) + W (TN rows x 128 B) as fit (up to 6).
+template <int TN>
+struct Tile {
+  static constexpr int B_BYTES = TN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (225 * 1024) / STAGE_BYTES < 6 ? (225 * 1024) / STAGE_BYTES : 6;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr uint32_t IDESC = umma_idesc_bf16(BM, TN, false, false);
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(TN % 32 == 0 && TN >= 128 && TN <= 256 && 2 * TN <= (int)TMEM_COLS, "tile width");
+};
 constexpr int HD = 128;  // head_dim of the QKV epilogue
 
 enum Epi : int { kPlain = 0, kSiluMul = 1, kQkvRope = 2 };
@@ -201,6 +209,7 @@ struct Fixup {
   int t;
 };
 
+template <int TN>
 __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, const Fixup& fx, int r_in, int col,
                                            float (&v)[32]) {
   uint32_t raw[32];
@@ -220,7 +229,7 @@ __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, cons
       continue;
     }
     const float4* src = reinterpret_cast<const float4*>(p.partials) +
-                        (int64_t)sk_slot(p, c, fx.t) * (BM * BN / 4) + (col / 4) * BM + r_in;
+                        (int64_t)sk_slot(p, c, fx.t) * (BM * TN / 4) + (col / 4) * BM + r_in;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float4 f = __ldcg(src + i * BM);
@@ -235,16 +244,16 @@ __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, cons
 // The epilogue of one accumulator tile: thread = row r_in of the tile (global row `row`),
 // output columns of tile nt.  Values come from this CTA's TMEM (`tacc`), plus the other
 // CTAs' partials in a stream-K fix-up (fx).
-template <int EPI>
+template <int EPI, int TN>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, const Fixup& fx, int r_in, int row,
                                               int nt) {
   const bool row_ok = row < p.m;
   if (EPI == kPlain) {
-    const int n0 = nt * BN;
+    const int n0 = nt * TN;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < TN / 32; ++c) {
       float v[32];
-      load_acc32(p, tacc + c * 32, fx, r_in, c * 32, v);
+      load_acc32<TN>(p, tacc + c * 32, fx, r_in, c * 32, v);
       const int col = n0 + c * 32;
       if (!row_ok || col >= p.n) continue;
       float b[32];
@@ -263,12 +272,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
     }
   } else if (EPI == kSiluMul) {
     // TMEM columns [0, 128): gate of output columns n0 + [0, 128); [128, 256): up.
-    const int n0 = nt * (BN / 2);
+    const int n0 = nt * (TN / 2);
 #pragma unroll 1
-    for (int c = 0; c < BN / 64; ++c) {
+    for (int c = 0; c < TN / 64; ++c) {
       float g[32], u[32];
-      load_acc32(p, tacc + c * 32, fx, r_in, c * 32, g);
-      load_acc32(p, tacc + BN / 2 + c * 32, fx, r_in, BN / 2 + c * 32, u);
+      load_acc32<TN>(p, tacc + c * 32, fx, r_in, c * 32, g);
+      load_acc32<TN>(p, tacc + TN / 2 + c * 32, fx, r_in, TN / 2 + c * 32, u);
       const int col = n0 + c * 32;
       if (!row_ok || col >= p.n) continue;
       uint32_t w[16];
@@ -294,7 +303,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
       }
     }
   } else {
-    // kQkvRope: the tile's 256 columns are two heads of the [q | k | v] layout.
+    // kQkvRope: the tile's TN columns are TN / 128 heads of the [q | k | v] layout.
     int64_t pos = 0, slot = -1;
     bool pos_ok = false, slot_ok = false;
     if (row_ok) {
@@ -304,8 +313,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
       slot_ok = slot >= -1 && slot < p.num_slots;
     }
 #pragma unroll 1
-    for (int hh = 0; hh < 2; ++hh) {
-      const int head = nt * 2 + hh;
+    for (int hh = 0; hh < TN / HD; ++hh) {
+      const int head = nt * (TN / HD) + hh;
       const bool is_q = head < p.num_heads;
       const bool is_v = head >= p.num_heads + p.num_kv_heads;
       const int col0 = head * HD;
@@ -314,8 +323,8 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
 #pragma unroll 1
       for (int r = 0; r < 2; ++r) {
         float x1[32], x2[32];
-        load_acc32(p, tacc + hh * HD + r * 32, fx, r_in, hh * HD + r * 32, x1);
-        load_acc32(p, tacc + hh * HD + 64 + r * 32, fx, r_in, hh * HD + 64 + r * 32, x2);
+        load_acc32<TN>(p, tacc + hh * HD + r * 32, fx, r_in, hh * HD + r * 32, x1);
+        load_acc32<TN>(p, tacc + hh * HD + 64 + r * 32, fx, r_in, hh * HD + 64 + r * 32, x2);
         if (!row_ok || col0 >= p.n) continue;
         if (!slot_ok || (!is_v && !pos_ok)) {
           if (hh == 0 && r == 0) record_error(!slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
@@ -368,17 +377,18 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
   }
 }
 
-template <int EPI>
+template <int EPI, int TN>
 __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
+  using TL = Tile<TN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = full + 2 * STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TL::OFF_BAR);
+  uint64_t* empty = full + TL::STAGES;
+  uint64_t* acc_full = full + 2 * TL::STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
-  volatile int* ticket_last = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TL::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TL::OFF_MISC + 4);
+  volatile int* ticket_last = reinterpret_cast<volatile int*>(smem + TL::OFF_MISC + 8);
   const int warp = warp_id(), lane = lane_id();
 
   if (warp == 1) {
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
   }
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < TL::STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
@@ -416,21 +426,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       for (bool more = seg_first(p, sg); ok && more; more = seg_next(p, sg)) {
         const int mt = sg.tile % p.m_tiles, nt = sg.tile / p.m_tiles;
         for (int kb = sg.kb_lo; kb < sg.kb_hi; ++kb, ++it) {
-          const int s = it % STAGES;
-          if (it >= STAGES &&
-              !wait_bar(empty + s, (uint32_t)((it / STAGES) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 40, abort_flag)) {
+          const int s = it % TL::STAGES;
+          if (it >= TL::STAGES &&
+              !wait_bar(empty + s, (uint32_t)((it / TL::STAGES) & 1) ^ 1u, VLC_DEV_ERR_TIMEOUT + 40, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = smem + s * STAGE_BYTES;
+          uint8_t* a_dst = smem + s * TL::STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
-          mbar_expect_tx(full + s, STAGE_BYTES);
+          mbar_expect_tx(full + s, TL::STAGE_BYTES);
           tma_load_2d(a_dst, &p.tm_a, full + s, kb * BK, mt * BM);
           if (EPI == kSiluMul) {
-            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * (BN / 2));
-            tma_load_2d(b_dst + B_BYTES / 2, &p.tm_b, full + s, kb * BK, p.up_row0 + nt * (BN / 2));
+            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * (TN / 2));
+            tma_load_2d(b_dst + TL::B_BYTES / 2, &p.tm_b, full + s, kb * BK, p.up_row0 + nt * (TN / 2));
           } else {
-            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * BN);
+            tma_load_2d(b_dst, &p.tm_b, full + s, kb * BK, nt * TN);
           }
         }
       }
@@ -451,19 +461,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)buf * BN;
+        const uint32_t d = tmem_base + (uint32_t)buf * TN;
         for (int kb = sg.kb_lo; kb < sg.kb_hi; ++kb, ++it) {
-          const int s = it % STAGES;
-          if (!wait_bar(full + s, (uint32_t)(it / STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 42, abort_flag)) {
+          const int s = it % TL::STAGES;
+          if (!wait_bar(full + s, (uint32_t)(it / TL::STAGES) & 1u, VLC_DEV_ERR_TIMEOUT + 42, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_lo = base_lo + (uint32_t)((s * STAGE_BYTES) >> 4);
+          const uint32_t a_lo = base_lo + (uint32_t)((s * TL::STAGE_BYTES) >> 4);
           const uint32_t b_lo = a_lo + (uint32_t)(A_BYTES >> 4);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_ss_w(d, a_lo + (uint32_t)(k * 2), hi, b_lo + (uint32_t)(k * 2), hi, IDESC,
+            umma_ss_w(d, a_lo + (uint32_t)(k * 2), hi, b_lo + (uint32_t)(k * 2), hi, TL::IDESC,
                       (kb > sg.kb_lo || k > 0) ? 1u : 0u);
           umma_commit(empty + s);
         }
@@ -487,7 +497,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       if (!wait_bar(acc_full + buf, (uint32_t)(local >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 43, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
-      const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
+      const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * TN;
       const int row = mt * BM + r_in;
       Fixup fx;
       fx.t = t;
@@ -498,9 +508,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
         // Partial layout: 16-byte piece q (columns 4q .. 4q + 3) of row r at float4 index
         // q * 128 + r, so one warp instruction stores (or loads) 512 contiguous bytes.
         float4* dst = reinterpret_cast<float4*>(p.partials) +
-                      (int64_t)(sg.index == 0 ? 2 * blockIdx.x : 2 * blockIdx.x + 1) * (BM * BN / 4) + r_in;
+                      (int64_t)(sg.index == 0 ? 2 * blockIdx.x : 2 * blockIdx.x + 1) * (BM * TN / 4) + r_in;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < TN / 32; ++c) {
           uint32_t v[32];
           tmem_ld32(tacc + c * 32, v);
           tmem_wait_ld();
@@ -532,7 +542,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
         fx.c_lo = c_lo;
         fx.c_hi = c_hi;
       }
-      epilogue_tile<EPI>(p, tacc, fx, r_in, row, nt);
+      epilogue_tile<EPI, TN>(p, tacc, fx, r_in, row, nt);
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
       if (*abort_flag) break;
@@ -691,7 +701,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
       __syncwarp();
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
-      epilogue_tile<EPI>(p, tacc, fx, r_in, mt * PM + (int)rank * BM + r_in, nt);
+      epilogue_tile<EPI, BN>(p, tacc, fx, r_in, mt * PM + (int)rank * BM + r_in, nt);
       tc_fence_before();
       if (rank == 0)
         mbar_arrive(acc_empty + buf);
@@ -709,10 +719,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
   }
 }
 
-// Tiles of an output of m x n (kSiluMul: n = intermediate size, 128 output columns a tile).
-inline void tile_counts(int kind, int m, int n, int k, int& m_tiles, int& n_tiles, int& k_blocks) {
+// Tiles of an output of m x n with tiles TN wide (kSiluMul: n = intermediate size, TN / 2
+// output columns a tile).
+inline void tile_counts(int kind, int m, int n, int k, int& m_tiles, int& n_tiles, int& k_blocks, int tn = BN) {
   m_tiles = (m + BM - 1) / BM;
-  n_tiles = kind == kSiluMul ? (n + BN / 2 - 1) / (BN / 2) : (n + BN - 1) / BN;
+  n_tiles = kind == kSiluMul ? (n + tn / 2 - 1) / (tn / 2) : (n + tn - 1) / tn;
   k_blocks = (k + BK - 1) / BK;
 }
 
@@ -734,9 +745,10 @@ int64_t workspace_bytes(int kind, int m, int n, int k) {
   return partials_bytes(std::max(1, vlc_num_sms())) + (tiles * 4 + 255) / 256 * 256;
 }
 
-template <int EPI>
+template <int EPI, int TN>
 int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t w_rows, void* workspace,
            int64_t ws_bytes, void* stream) {
+  using TL = Tile<TN>;
   {
     const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)prm.m};
     const uint64_t strides[1] = {(uint64_t)lda * 2};
@@ -746,10 +758,10 @@ int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, 
   {
     const uint64_t dims[2] = {(uint64_t)prm.k, (uint64_t)w_rows};
     const uint64_t strides[1] = {(uint64_t)ldw * 2};
-    const uint32_t box[2] = {BK, (uint32_t)(EPI == kSiluMul ? BN / 2 : BN)};
+    const uint32_t box[2] = {BK, (uint32_t)(EPI == kSiluMul ? TN / 2 : TN)};
     if (encode_tmap_bf16(&prm.tm_b, w, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
   }
-  tile_counts(EPI, prm.m, prm.n, prm.k, prm.m_tiles, prm.n_tiles, prm.k_blocks);
+  tile_counts(EPI, prm.m, prm.n, prm.k, prm.m_tiles, prm.n_tiles, prm.k_blocks, TN);
   prm.tiles = prm.m_tiles * prm.n_tiles;
   prm.total_kb = (int64_t)prm.tiles * prm.k_blocks;
   const int sms = std::max(1, vlc_num_sms());
@@ -773,25 +785,27 @@ int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, 
     prm.partials = nullptr;
   }
   static std::atomic<uint64_t> smem_set{0};
-  if (ensure_dynamic_smem((const void*)gemm_kernel<EPI>, SMEM_BYTES, smem_set) != VLC_OK) return VLC_ERR_CUDA;
+  if (ensure_dynamic_smem((const void*)gemm_kernel<EPI, TN>, TL::SMEM_BYTES, smem_set) != VLC_OK)
+    return VLC_ERR_CUDA;
   cudaLaunchAttribute pdl;
   pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   pdl.val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(NUM_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = TL::SMEM_BYTES;
   cfg.stream = (cudaStream_t)stream;
   cfg.attrs = &pdl;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, gemm_kernel<EPI>, prm) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, gemm_kernel<EPI, TN>, prm) != cudaSuccess) {
     (void)cudaGetLastError();
     return VLC_ERR_CUDA;
   }
   return VLC_OK;
 }
 
-// Kernel selection: 0 = automatic, 1 = single-SM tiles (stream-K where it pays), 2 = CTA pairs.
+// Kernel selection: 0 = automatic, 1 = single-SM 128 x 256 tiles (stream-K where it pays),
+// 2 = CTA pairs (256 x 256), 3 = single-SM 128 x 128, 4 = single-SM 128 x 224 (plain only).
 static std::atomic<int> g_kernel_mode{0};
 
 template <int EPI>
@@ -853,14 +867,69 @@ int launch_pair(Params& prm, const void* a, int64_t lda, const void* w, int64_t 
   return VLC_OK;
 }
 
-// Which kernel runs a launch: the pair kernel unless single-SM tiles are asked for or the
-// stream-K split applies (workspace given and tiles few and long).
+// Automatic configuration: the one whose launch is estimated to end first.  Model (cycles,
+// fitted to B200 timings of the 1,123-row projections of Qwen2.5-VL-3B / 7B, 32-296 K
+// blocks, all four configurations): the tiles run in waves of one tile per SM (or SM
+// pair); a wave with `act` SMs busy costs k_blocks * (f + s * act) -- the operands of
+// every busy SM come through the shared L2, so a K block gets slower the more SMs load at
+// once -- and the first wave adds the fill / drain / epilogue cost of a tile (later waves
+// a fifth of it: the next tile's MMAs overlap the previous epilogue).
+struct Cfg {
+  int mode, tm, tn;  // vlc_linear_set_kernel mode, tile rows, tile columns (output)
+  int per_unit;      // SMs per unit of work (2: CTA pairs)
+  double tile, f, s;
+};
+constexpr Cfg kCfgs[] = {
+    {2, 2 * BM, BN, 2, 9400.0, 483.0, 1.87},  // CTA pairs, 256 x 256
+    {1, BM, 256, 1, 8300.0, 762.0, 0.0},      // single SM, 128 x 256
+    {4, BM, 224, 1, 8500.0, 583.0, 0.67},     // single SM, 128 x 224 (plain epilogue)
+    {3, BM, 128, 1, 9600.0, 400.0, 1.03},     // single SM, 128 x 128 (plain, QKV)
+};
+
+inline double estimate_cycles(const Cfg& c, int kind, int m, int n, int k_blocks, int sms) {
+  const int units = std::max(1, sms / c.per_unit);
+  const int cols = kind == kSiluMul ? c.tn / 2 : c.tn;
+  int64_t left = (int64_t)((m + c.tm - 1) / c.tm) * ((n + cols - 1) / cols);
+  double t = 0.0;
+  for (int wave = 0; left > 0; ++wave, left -= units) {
+    const double act = (double)std::min<int64_t>(left, units) * c.per_unit;
+    t += (wave == 0 ? c.tile : 0.2 * c.tile) + k_blocks * (c.f + c.s * act);
+  }
+  return t;
+}
+
+inline int auto_mode(int kind, int m, int n, int k) {
+  const int sms = std::max(2, vlc_num_sms());
+  const int k_blocks = (k + BK - 1) / BK;
+  double best = 1e300;
+  int best_mode = 2;
+  for (const Cfg& c : kCfgs) {
+    if (kind == kSiluMul && c.mode >= 3) continue;  // gate and up halves of 128 columns
+    if (kind == kQkvRope && c.mode == 4) continue;  // head-aligned tiles only
+    const double t = estimate_cycles(c, kind, m, n, k_blocks, sms);
+    if (t < best) {
+      best = t;
+      best_mode = c.mode;
+    }
+  }
+  return best_mode;
+}
+
+// Which kernel runs a launch: the configuration asked for (vlc_linear_set_kernel), or the
+// automatic one.
 template <int EPI>
 int dispatch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t w_rows, void* workspace,
              int64_t ws_bytes, void* stream) {
-  const int mode = g_kernel_mode.load();
-  if (mode == 2) return launch_pair<EPI>(prm, a, lda, w, ldw, w_rows, stream);
-  if (mode == 1) return launch<EPI>(prm, a, lda, w, ldw, w_rows, workspace, ws_bytes, stream);
+  int mode = g_kernel_mode.load();
+  // 128-wide tiles have no room for SiLU's gate and up halves, 224-wide ones split heads:
+  // those epilogues take the automatic choice instead.
+  if (mode == 0 || (mode == 3 && EPI == kSiluMul) || (mode == 4 && EPI != kPlain))
+    mode = auto_mode(EPI, prm.m, prm.n, prm.k);
+  if (mode == 1) return launch<EPI, 256>(prm, a, lda, w, ldw, w_rows, workspace, ws_bytes, stream);
+  if (mode == 3)
+    return launch<EPI, EPI == kSiluMul ? 256 : 128>(prm, a, lda, w, ldw, w_rows, workspace, ws_bytes, stream);
+  if (mode == 4)
+    return launch<EPI, EPI == kPlain ? 224 : 256>(prm, a, lda, w, ldw, w_rows, workspace, ws_bytes, stream);
   return launch_pair<EPI>(prm, a, lda, w, ldw, w_rows, stream);
 }
 
@@ -964,7 +1033,7 @@ extern "C" int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void
 }
 
 extern "C" int vlc_linear_set_kernel(int mode) {
-  if (mode < 0 || mode > 2) return VLC_ERR_UNSUPPORTED;
+  if (mode < 0 || mode > 4) return VLC_ERR_UNSUPPORTED;
   g_kernel_mode.store(mode);
   return VLC_OK;
 }

@@ -408,8 +408,10 @@ def linear_workspace(kind: int, m: int, n: int, k: int, device) -> tuple[torch.T
 
 
 def set_linear_kernel(mode: int) -> None:
-    """GEMM kernel of the linear ops, process-wide: 0 automatic, 1 single-SM tiles (stream-K
-    where it pays), 2 CTA pairs (tcgen05.mma.cta_group::2)."""
+    """GEMM kernel of the linear ops, process-wide: 0 automatic (a cost model picks per
+    shape), 1 single-SM 128 x 256 tiles (stream-K where it pays), 2 CTA pairs
+    (tcgen05.mma.cta_group::2, 256 x 256), 3 single-SM 128 x 128, 4 single-SM 128 x 224
+    (plain linear only; the fused epilogues fall back to pairs)."""
     check("vlc_linear_set_kernel", lib().vlc_linear_set_kernel(int(mode)))
 
 
