@@ -59,10 +59,12 @@ struct Tile {
   static constexpr int STAGES = (225 * 1024) / STAGE_BYTES < 6 ? (225 * 1024) / STAGE_BYTES : 6;
   static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 4;  // full[S], empty[S], acc_full[2], acc_empty[2]
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int OFF_MISC = (OFF_BAR + NUM_BARS * 8 + 127) / 128 * 128;
+  static constexpr int OFF_BIAS = OFF_MISC + 64;   // each epilogue warp's copy of the tile's bias
+  static constexpr int SMEM_BYTES = OFF_BIAS + 4 * 256 * 2 + 1024;
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, TN, false, false);
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(OFF_BIAS % 16 == 0, "alignment of the bias copies");
   static_assert(TN % 32 == 0 && TN >= 128 && TN <= 256 && 2 * TN <= (int)TMEM_COLS, "tile width");
 };
 constexpr int HD = 128;  // head_dim of the QKV epilogue
@@ -123,26 +125,87 @@ __device__ __forceinline__ void store32(__nv_bfloat16* dst, const uint32_t (&w)[
   for (int i = 0; i < 4; ++i) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
 
-// Bias of 32 consecutive columns starting at `col` (0 when null or at columns >= n),
-// as fp32; n is a multiple of 8, so a group of 8 columns is wholly inside or outside.
-__device__ __forceinline__ void load_bias32(const __nv_bfloat16* bias, int col, int n, float (&b)[32]) {
-  if (bias == nullptr) {
+// The tile's bias (tile columns [0, TN) = output columns n0 + [0, TN)) copied by one
+// epilogue warp into its own shared-memory buffer, with zeros at columns >= n (n is a
+// multiple of 8, so a group of 8 columns is wholly inside or outside).  Issued before the
+// tile's accumulator is ready, so its global-memory round trip overlaps the main loop;
+// each warp has its own copy, so only the warp itself synchronises on it.
+template <int TN>
+__device__ __forceinline__ void stage_bias(const __nv_bfloat16* bias, int n0, int n, __nv_bfloat16* bias_s) {
+  const int lane = lane_id();
+  __syncwarp();  // every lane is done with the previous tile's copy
+  if (lane < TN / 8) {
+    const int col = n0 + 8 * lane;
+    const uint4 u = col < n ? __ldg(reinterpret_cast<const uint4*>(bias + col)) : make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(bias_s)[lane] = u;
+  }
+  __syncwarp();
+}
+
+// 8 bias values of tile columns [c, c + 8) from the warp's copy (zeros without a bias).
+__device__ __forceinline__ void bias8_smem(const __nv_bfloat16* bias_s, int c, float (&b)[8]) {
+  if (bias_s == nullptr) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) b[i] = 0.f;
+    for (int i = 0; i < 8; ++i) b[i] = 0.f;
     return;
   }
-  const uint4* s = reinterpret_cast<const uint4*>(bias + col);
+  const uint4 u = *reinterpret_cast<const uint4*>(bias_s + c);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 u = col + 8 * i < n ? __ldg(s + i) : make_uint4(0, 0, 0, 0);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-      b[8 * i + 2 * j] = f.x;
-      b[8 * i + 2 * j + 1] = f.y;
-    }
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+    b[2 * j] = f.x;
+    b[2 * j + 1] = f.y;
   }
+}
+
+// Loads as volatile asm: issued where they stand (before the accumulator wait, itself
+// volatile asm), not moved by the compiler to their first use after it.
+__device__ __forceinline__ float4 ld_nc_early(const float4* ptr) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ int64_t ld_nc_early(const int64_t* ptr) {
+  int64_t v;
+  asm volatile("ld.global.nc.s64 %0, [%1];" : "=l"(v) : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ int32_t ld_nc_early(const int32_t* ptr) {
+  int32_t v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(ptr));
+  return v;
+}
+
+// Per-row inputs of the QKV epilogue, loaded before the tile's accumulator is ready so
+// that no global-memory round trip is left between the last MMA and the stores: the
+// row's position and cache slot, and its 64 cos and 64 sin values (one table row, shared
+// by every q and k head of the row).
+struct QkvRow {
+  int64_t slot;
+  bool row_ok, pos_ok, slot_ok;
+  float4 cs[32];  // cos[0, 64) in cs[0, 16), sin[0, 64) in cs[16, 32)
+};
+
+template <int EPI>
+__device__ __forceinline__ void qkv_prefetch(const Params& p, int row, QkvRow& q) {
+  if (EPI != kQkvRope) return;
+  q.row_ok = row < p.m;
+  q.slot = -1;
+  q.pos_ok = q.slot_ok = false;
+  int64_t pos = 0;
+  if (q.row_ok) {
+    pos = ld_nc_early(p.positions + row);
+    q.slot = ld_nc_early(p.slot_mapping + row);
+    q.pos_ok = pos >= 0 && pos < p.max_position;
+    q.slot_ok = q.slot >= -1 && q.slot < p.num_slots;
+  }
+  // an invalid position reads table row 0 (the values are then not used)
+  const float4* cs = reinterpret_cast<const float4*>(p.cos_sin + (q.pos_ok ? pos : 0) * HD);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) q.cs[i] = ld_nc_early(cs + i);
 }
 
 // A CTA's work as segments: (tile, first K block, end K block).  Stream-K: the CTA's
@@ -243,10 +306,11 @@ __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, cons
 
 // The epilogue of one accumulator tile: thread = row r_in of the tile (global row `row`),
 // output columns of tile nt.  Values come from this CTA's TMEM (`tacc`), plus the other
-// CTAs' partials in a stream-K fix-up (fx).
+// CTAs' partials in a stream-K fix-up (fx).  bias_s is the warp's copy of the tile's bias
+// (stage_bias) or null; qr the row's prefetched QKV inputs (qkv_prefetch).
 template <int EPI, int TN>
 __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, const Fixup& fx, int r_in, int row,
-                                              int nt) {
+                                              int nt, const __nv_bfloat16* bias_s, const QkvRow& qr) {
   const bool row_ok = row < p.m;
   if (EPI == kPlain) {
     const int n0 = nt * TN;
@@ -256,11 +320,14 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
       load_acc32<TN>(p, tacc + c * 32, fx, r_in, c * 32, v);
       const int col = n0 + c * 32;
       if (!row_ok || col >= p.n) continue;
-      float b[32];
-      load_bias32(p.bias, col, p.n, b);
       uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) w[i] = pack2(v[2 * i] + b[2 * i], v[2 * i + 1] + b[2 * i + 1]);
+      for (int g = 0; g < 4; ++g) {
+        float b[8];
+        bias8_smem(bias_s, c * 32 + 8 * g, b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[4 * g + i] = pack2(v[8 * g + 2 * i] + b[2 * i], v[8 * g + 2 * i + 1] + b[2 * i + 1]);
+      }
       __nv_bfloat16* dst = p.out + (int64_t)row * p.ldo + col;
       if (col + 32 <= p.n) {
         store32(dst, w);
@@ -303,56 +370,62 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
       }
     }
   } else {
-    // kQkvRope: the tile's TN columns are TN / 128 heads of the [q | k | v] layout.
-    int64_t pos = 0, slot = -1;
-    bool pos_ok = false, slot_ok = false;
-    if (row_ok) {
-      pos = __ldg(p.positions + row);
-      slot = __ldg(p.slot_mapping + row);
-      pos_ok = pos >= 0 && pos < p.max_position;
-      slot_ok = slot >= -1 && slot < p.num_slots;
-    }
+    // kQkvRope (whole tiles only: the accumulator is this CTA's): the tile's TN columns are
+    // TN / 128 heads of the [q | k | v] layout.  Each head's 128 columns go in four steps
+    // of (x1: 16 columns of the first half, x2: the matching 16 of the second half); step
+    // j of every head uses the row's cos / sin values [16 j, 16 j + 16), prefetched in qr.
 #pragma unroll 1
     for (int hh = 0; hh < TN / HD; ++hh) {
       const int head = nt * (TN / HD) + hh;
       const bool is_q = head < p.num_heads;
       const bool is_v = head >= p.num_heads + p.num_kv_heads;
       const int col0 = head * HD;
-      // the head's 128 columns in two rounds of (x1: 32 of the first half, x2: the
-      // matching 32 of the second half)
-#pragma unroll 1
-      for (int r = 0; r < 2; ++r) {
-        float x1[32], x2[32];
-        load_acc32<TN>(p, tacc + hh * HD + r * 32, fx, r_in, hh * HD + r * 32, x1);
-        load_acc32<TN>(p, tacc + hh * HD + 64 + r * 32, fx, r_in, hh * HD + 64 + r * 32, x2);
-        if (!row_ok || col0 >= p.n) continue;
-        if (!slot_ok || (!is_v && !pos_ok)) {
-          if (hh == 0 && r == 0) record_error(!slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x1[16], x2[16];
+        {
+          uint32_t a1[16], a2[16];
+          tmem_ld16(tacc + hh * HD + 16 * j, a1);
+          tmem_ld16(tacc + hh * HD + 64 + 16 * j, a2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            x1[i] = __uint_as_float(a1[i]);
+            x2[i] = __uint_as_float(a2[i]);
+          }
+        }
+        // (tcgen05.ld is warp-collective: rows past m load too, and write nothing)
+        if (!qr.row_ok || col0 >= p.n) continue;
+        if (!qr.slot_ok || (!is_v && !qr.pos_ok)) {
+          if (hh == 0 && j == 0) record_error(!qr.slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
           continue;
         }
         __nv_bfloat16* dst;
         if (is_q) {
           dst = p.q_out + (int64_t)row * p.q_out_stride + (int64_t)head * HD;
         } else {
-          if (slot < 0) continue;
+          if (qr.slot < 0) continue;
           const int kvh = is_v ? head - p.num_heads - p.num_kv_heads : head - p.num_heads;
-          dst = (is_v ? p.v_cache : p.k_cache) + slot * ((int64_t)p.num_kv_heads * HD) + (int64_t)kvh * HD;
+          dst = (is_v ? p.v_cache : p.k_cache) + qr.slot * ((int64_t)p.num_kv_heads * HD) + (int64_t)kvh * HD;
         }
-        float bx[32], by[32];
-        load_bias32(p.bias, col0 + r * 32, p.n, bx);
-        load_bias32(p.bias, col0 + 64 + r * 32, p.n, by);
+        // the linear's bf16 output: acc + bias, rounded (bias 8 columns at a time)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x1[i] = bf16_round(x1[i] + bx[i]);  // the linear's bf16 output
-          x2[i] = bf16_round(x2[i] + by[i]);
+        for (int g = 0; g < 2; ++g) {
+          float bx[8], by[8];
+          bias8_smem(bias_s, hh * HD + 16 * j + 8 * g, bx);
+          bias8_smem(bias_s, hh * HD + 64 + 16 * j + 8 * g, by);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            x1[8 * g + e] = bf16_round(x1[8 * g + e] + bx[e]);
+            x2[8 * g + e] = bf16_round(x2[8 * g + e] + by[e]);
+          }
         }
         if (!is_v) {
           // apply_rotary_emb in fp32, each product and sum rounded on its own
-          const float* cs = p.cos_sin + pos * HD;
 #pragma unroll
-          for (int i4 = 0; i4 < 8; ++i4) {
-            const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + r * 32) + i4);
-            const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + 64 + r * 32) + i4);
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 c4 = qr.cs[4 * j + i4];
+            const float4 s4 = qr.cs[16 + 4 * j + i4];
             const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -364,14 +437,18 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
             }
           }
         }
-        uint32_t w1[16], w2[16];
+        uint32_t w1[8], w2[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           w1[i] = pack2(x1[2 * i], x1[2 * i + 1]);
           w2[i] = pack2(x2[2 * i], x2[2 * i + 1]);
         }
-        store32(dst + r * 32, w1);
-        store32(dst + 64 + r * 32, w2);
+        uint4* o1 = reinterpret_cast<uint4*>(dst + 16 * j);
+        uint4* o2 = reinterpret_cast<uint4*>(dst + 64 + 16 * j);
+        o1[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+        o1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
+        o2[0] = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+        o2[1] = make_uint4(w2[4], w2[5], w2[6], w2[7]);
       }
     }
   }
@@ -488,22 +565,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
     const int r_in = quarter * 32 + lane;     // tile row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const bool leader = warp == 2 && lane == 0;
+    __nv_bfloat16* bias_s =
+        p.bias != nullptr ? reinterpret_cast<__nv_bfloat16*>(smem + TL::OFF_BIAS) + (warp - 2) * 256 : nullptr;
+    QkvRow qr;
     int local = 0;
     SegIter sg;
     for (bool more = seg_first(p, sg); more; more = seg_next(p, sg), ++local) {
       const int t = sg.tile;
       const int mt = t % p.m_tiles, nt = t / p.m_tiles;
       const int buf = local & 1;
+      const int row = mt * BM + r_in;
+      // inputs of the epilogue that do not depend on the accumulator: loaded while the MMAs run
+      if (bias_s != nullptr) stage_bias<TN>(p.bias, nt * TN, p.n, bias_s);
+      qkv_prefetch<EPI>(p, row, qr);
       if (!wait_bar(acc_full + buf, (uint32_t)(local >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 43, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * TN;
-      const int row = mt * BM + r_in;
       Fixup fx;
       fx.t = t;
       fx.c_lo = 1;
       fx.c_hi = 0;  // no partials to add
-      if (sg.kb_lo != 0 || sg.kb_hi != p.k_blocks) {
+      if (EPI != kQkvRope && (sg.kb_lo != 0 || sg.kb_hi != p.k_blocks)) {
         // Stream-K: this CTA covers part of the tile.  Leave the partial, take a ticket.
         // Partial layout: 16-byte piece q (columns 4q .. 4q + 3) of row r at float4 index
         // q * 128 + r, so one warp instruction stores (or loads) 512 contiguous bytes.
@@ -542,7 +625,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
         fx.c_lo = c_lo;
         fx.c_hi = c_hi;
       }
-      epilogue_tile<EPI, TN>(p, tacc, fx, r_in, row, nt);
+      epilogue_tile<EPI, TN>(p, tacc, fx, r_in, row, nt, bias_s, qr);
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
       if (*abort_flag) break;
@@ -577,9 +660,11 @@ constexpr int PB_BYTES = 128 * BK * 2;            // 16 KB: this CTA's rows of W
 constexpr int PSTAGE = PA_BYTES + PB_BYTES;       // 32 KB
 constexpr int P_OFF_BAR = PAIR_STAGES * PSTAGE;
 constexpr int P_NUM_BARS = 2 * PAIR_STAGES + 4;
-constexpr int P_OFF_MISC = P_OFF_BAR + P_NUM_BARS * 8;
-constexpr int P_SMEM_BYTES = P_OFF_MISC + 16 + 1024;
+constexpr int P_OFF_MISC = (P_OFF_BAR + P_NUM_BARS * 8 + 127) / 128 * 128;
+constexpr int P_OFF_BIAS = P_OFF_MISC + 64;
+constexpr int P_SMEM_BYTES = P_OFF_BIAS + 4 * 256 * 2 + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(P_OFF_BIAS % 16 == 0, "alignment of the bias copies");
 constexpr uint32_t IDESC_PAIR = umma_idesc_bf16(2 * BM, BN, false, false);
 constexpr int PM = 2 * BM;  // output rows of a pair tile
 
@@ -693,15 +778,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
     fx.t = 0;
     fx.c_lo = 1;
     fx.c_hi = 0;
+    __nv_bfloat16* bias_s =
+        p.bias != nullptr ? reinterpret_cast<__nv_bfloat16*>(smem + P_OFF_BIAS) + (warp - 2) * 256 : nullptr;
+    QkvRow qr;
     int local = 0;
     for (int t = pair; t < p.tiles; t += npairs, ++local) {
       const int mt = t % p.m_tiles, nt = t / p.m_tiles;
       const int buf = local & 1;
+      const int row = mt * PM + (int)rank * BM + r_in;
+      if (bias_s != nullptr) stage_bias<BN>(p.bias, nt * BN, p.n, bias_s);
+      qkv_prefetch<EPI>(p, row, qr);
       if (!wait_bar(acc_full + buf, (uint32_t)(local >> 1) & 1u, VLC_DEV_ERR_TIMEOUT + 47, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
       const uint32_t tacc = tmem_base + lane_off + (uint32_t)buf * BN;
-      epilogue_tile<EPI, BN>(p, tacc, fx, r_in, mt * PM + (int)rank * BM + r_in, nt);
+      epilogue_tile<EPI, BN>(p, tacc, fx, r_in, row, nt, bias_s, qr);
       tc_fence_before();
       if (rank == 0)
         mbar_arrive(acc_empty + buf);
@@ -769,7 +860,8 @@ int launch(Params& prm, const void* a, int64_t lda, const void* w, int64_t ldw, 
   // enough (>= 64 K blocks) to amortise the partial write and the fix-up (measured on
   // B200: down_proj of 1,123 rows, K = 11,008, 72 tiles: 59.8 vs 67.8 us; qkv_proj, K =
   // 2,048, 90 tiles: 30.8 vs 17.8 us); elsewhere the workspace is left unused.
-  const bool split = prm.tiles * 4 < sms * 3 && prm.k_blocks >= 64;
+  // The QKV epilogue takes whole tiles only.
+  const bool split = EPI != kQkvRope && prm.tiles * 4 < sms * 3 && prm.k_blocks >= 64;
   int grid;
   if (workspace != nullptr && split) {
     // Stream-K needs the whole workspace (tickets zeroed by the caller once; every launch
