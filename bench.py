@@ -776,12 +776,15 @@ def encoder_hash_bench(device, hbm_peak, reps: int = 20):
 
 
 # ---------------------------------------------------------------------------- vision attention
-def vision_attention_bench(device, tf_peak, reps: int = 5):
+def vision_attention_bench(device, tf_peak, reps: int = 5, hbm_peak: float | None = None):
     """The vision tower's attention for one 4K image (77 x 137 merged grid, 42,196
     patches, 16 heads of 80; nanovllm/models/qwen2_5_vl.py:202-211): a window block
     (windows of 4 x 4 merged tokens = 64 patches, ragged at the borders) and a
     full-attention block, non-causal, on the tcgen05 kernel and on flash-attn (the
-    reference's call) with the same inputs.  FLOP = 4 x 80 x 16 x sum of q.k pairs."""
+    reference's call) with the same inputs.  FLOP = 4 x 80 x 16 x sum of q.k pairs;
+    bytes = q, k, v read and O written once (4 x patches x 16 x 80 x 2 B = 432 MB).  The
+    window block's arithmetic intensity (≈32 FLOP/B) is below the B200's ridge, so its
+    roofline is HBM (`hbm_frac`); the full block's is the tensor pipe (`frac`)."""
     from vlcache_b200 import ops
     from vlcache_b200.layers.vision_attention import plan_varlen
     gh, gw, H, d = 77, 137, 16, 80
@@ -810,8 +813,12 @@ def vision_attention_bench(device, tf_peak, reps: int = 5):
         def ours():
             ops.prefill_attention(q, k, v, None, plan, scale, out, ws)
         ms = timed(graph_of(ours).replay, reps, 2, False)
+        nbytes = 4 * n * H * d * 2
         r = {"windows": len(lens), "us": ms * 1e3, "tflops": flop / (ms * 1e-3) / 1e12,
-             "frac": flop / (ms * 1e-3) / 1e12 / tf_peak, "flop": flop}
+             "frac": flop / (ms * 1e-3) / 1e12 / tf_peak, "flop": flop, "bytes": nbytes,
+             "hbm_gbs": nbytes / (ms * 1e-3) / 1e9}
+        if hbm_peak:
+            r["hbm_frac"] = r["hbm_gbs"] / hbm_peak
         if fa is not None:
             mx = int(max(lens))
 
@@ -980,7 +987,7 @@ def run_only(args, device):
         torch.cuda.synchronize()
         res["wall_ms"] = (time.perf_counter() - t0) * 1e3
     elif args.only == "vision":
-        res["vision_attention"] = vision_attention_bench(device, peaks()[1], reps=max(1, args.steps))
+        res["vision_attention"] = vision_attention_bench(device, peaks()[1], reps=max(1, args.steps), hbm_peak=peaks()[0])
     elif args.only == "hash":
         res["encoder_hash"] = encoder_hash_bench(device, peaks()[0], reps=max(1, args.steps))
     elif args.only == "linear":
@@ -1161,7 +1168,7 @@ def main():
     cfg1 = cfg1_bench(device) if rank == 0 else None
     lin = linear_bench(device, tf_peak) if rank == 0 else None
     ehash = encoder_hash_bench(device, hbm_peak) if rank == 0 else None
-    vit = vision_attention_bench(device, tf_peak) if rank == 0 else None
+    vit = vision_attention_bench(device, tf_peak, hbm_peak=hbm_peak) if rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
