@@ -336,7 +336,8 @@ int vlc_linear_silu_mul(const void* x, int64_t ldx, const void* gate_up_weight, 
  *   Replaces qkv_proj -> rotary_emb -> store_kvcache
  *   (nanovllm/models/qwen3.py:75-84, rotary_embedding.py:37-48, attention.py:10-40).
  * Out-of-range slots / positions are recorded as VLC_DEV_ERR_SLOT_RANGE /
- * VLC_DEV_ERR_POSITION and the row's stores skipped. */
+ * VLC_DEV_ERR_POSITION and the row's stores skipped.  Whole output tiles only:
+ * the workspace arguments are accepted and left untouched. */
 int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weight, int64_t ldw,
                                const void* qkv_bias, const int64_t* positions, const float* cos_sin_cache,
                                int64_t max_position, void* q_out, int64_t q_out_stride, void* k_cache,
