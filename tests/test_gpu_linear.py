@@ -192,6 +192,44 @@ def test_qkv_rope_store_bit_exact_vs_unfused(kernel_mode, margins, H, Hk, hidden
                       f"qkv_rope v cache (H={H})", margins)
 
 
+def test_qkv_rope_store_errors_match_unfused(kernel_mode):
+    """Rows with an out-of-range rotary position or cache slot: the fused kernel records
+    the same device error as the RoPE + scatter kernel and leaves the same outputs (a bad
+    position skips the row's q and k, a bad slot its k and v), bit for bit."""
+    from vlcache_b200 import ops
+    from vlcache_b200.layers.rotary_embedding import rope_cos_sin_cache
+    D, H, Hk, hidden, m, max_pos, num_slots = 128, 16, 2, 256, 300, 512, 512
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(m, hidden, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((H + 2 * Hk) * D, hidden, generator=g, device="cuda") / 16).to(torch.bfloat16)
+    b = torch.randn((H + 2 * Hk) * D, generator=g, device="cuda").to(torch.bfloat16)
+    table = rope_cos_sin_cache(D, max_pos, 1e6).to("cuda")
+    kc0 = torch.randn(num_slots // 256, 256, Hk, D, generator=g, device="cuda").to(torch.bfloat16)
+    qkv = ops.linear(x, w, b)
+    for bad, code in (("pos", 103), ("slot", 101)):
+        pos = torch.randint(0, max_pos, (m,), generator=g, device="cuda")
+        slots = torch.randperm(num_slots, generator=g, device="cuda")[:m].to(torch.int32)
+        if bad == "pos":
+            pos[[5, 130, 299]] = max_pos
+        else:
+            slots[[7, 200]] = num_slots
+        outs = []
+        for fused in (True, False):
+            kc, vc = kc0.clone(), kc0.clone()
+            q = torch.full((m, H, D), 7.0, dtype=torch.bfloat16, device="cuda")
+            ops.device_error(reset=True)
+            if fused:
+                ops.qkv_rope_store_kvcache(x, w, b, pos, table, kc, vc, slots, H, Hk, q_out=q)
+            else:
+                ops.rope_store_kvcache(pos, qkv[:, :H * D].view(m, H, D), qkv[:, H * D:(H + Hk) * D].view(m, Hk, D),
+                                       qkv[:, (H + Hk) * D:].view(m, Hk, D), table, kc, vc, slots, out=q)
+            torch.cuda.synchronize()
+            assert ops.device_error(reset=True) == code, (bad, fused)
+            outs.append((q, kc, vc))
+        for a, c in zip(*outs):
+            assert torch.equal(a.view(torch.int16), c.view(torch.int16)), bad
+
+
 def _assert_rope_close(out, ref, x_pre, what, margins):
     """A rotation y1 = x1 c - x2 s, y2 = x2 c + x1 s of bf16 inputs that may each differ by
     one ulp from the fp32 reference's rounding: |err| <= 2^-7 (|x1| + |x2|) of the pair's

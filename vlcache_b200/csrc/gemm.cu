@@ -396,8 +396,11 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
         }
         // (tcgen05.ld is warp-collective: rows past m load too, and write nothing)
         if (!qr.row_ok || col0 >= p.n) continue;
-        if (!qr.slot_ok || (!is_v && !qr.pos_ok)) {
-          if (hh == 0 && j == 0) record_error(!qr.slot_ok ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
+        // As vlc_rope_store_kvcache: a k or v row needs a valid slot, a q or k row a valid
+        // position; a row that has neither is recorded and not stored (q does not use the slot).
+        const bool bad_slot = !is_q && !qr.slot_ok, bad_pos = !is_v && !qr.pos_ok;
+        if (bad_slot || bad_pos) {
+          if (j == 0) record_error(bad_slot ? VLC_DEV_ERR_SLOT_RANGE : VLC_DEV_ERR_POSITION);
           continue;
         }
         __nv_bfloat16* dst;
