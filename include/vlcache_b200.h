@@ -351,13 +351,14 @@ int vlc_qkv_rope_store_kvcache(const void* x, int64_t ldx, const void* qkv_weigh
  * pixel bytes, on the host, called per image at nanovllm/engine/llm_engine.py:52)
  * with a tree of XXH64 whose leaves hash in parallel (same bytes -> same key):
  *   d1[i] = XXH64(data[1024 i, 1024 (i+1)), seed 1)      (last chunk shorter)
- *   d2[j] = XXH64(d1 as little-endian bytes [1024 j, 1024 (j+1)), seed 2)
+ *   d2[j] = XXH64(d1 as little-endian bytes [512 j, 512 (j+1)), seed 2)
+ *   d3[k] = XXH64(d2 as little-endian bytes [1024 k, 1024 (k+1)), seed 3)
  *   digest = XXH64(little-endian uint64 words {header_len, header zero-padded to a
- *            multiple of 8 bytes, nbytes, n1 = #d1, d2...}, seed 3)
+ *            multiple of 8 bytes, nbytes, n1 = #d1, d3...}, seed 4)
  * header: the caller's bytes (e.g. grid_thw as int64 x 3), at most 256.
  *
  * vlc_content_hash_device: data in device memory; digest (one uint64) written to
- *   device memory `digest` on `stream` (three launches); workspace of
+ *   device memory `digest` on `stream` (two launches); workspace of
  *   vlc_content_hash_workspace_size(nbytes) bytes, 16-byte aligned.
  * vlc_content_hash_host: data in host memory, level 1 split over num_threads
  *   threads (<= 0: all hardware threads); digest written to *digest.

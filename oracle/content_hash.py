@@ -10,8 +10,9 @@ module, as the checker; the product path never calls it.
   the ``xxhash`` package) pins it.
 * ``tree_hash`` is the library's parallel content hash built from that primitive
   (include/vlcache_b200.h, vlc_content_hash_*): level 1 XXH64 (seed 1) of 1 KB chunks,
-  level 2 XXH64 (seed 2) of the level-1 digests in 1 KB chunks, then XXH64 (seed 3) of
-  the little-endian words {header_len, header zero-padded to 8 bytes, nbytes, n1, d2...}.
+  level 2 XXH64 (seed 2) of the level-1 digests in 512-byte chunks (64 digests), level 3
+  XXH64 (seed 3) of the level-2 digests in 1 KB chunks, then XXH64 (seed 4) of the
+  little-endian words {header_len, header zero-padded to 8 bytes, nbytes, n1, d3...}.
 numpy uint64 arithmetic wraps like the C code; level 1 is vectorised over chunks.
 """
 from __future__ import annotations
@@ -87,18 +88,19 @@ def _np_round(acc, inp):
 
 
 def _xxh64_full_chunks(words: np.ndarray, seed: int) -> np.ndarray:
-    """XXH64 of each row of ``words`` [n, CHUNK // 8] (full 1 KB chunks), vectorised."""
-    n = words.shape[0]
+    """XXH64 of each row of ``words`` [n, chunk // 8] (full chunks of a multiple of 32
+    bytes), vectorised."""
+    n, nw = words.shape
     with np.errstate(over="ignore"):
         v = [np.full(n, (seed + P1 + P2) & M64, np.uint64), np.full(n, (seed + P2) & M64, np.uint64),
              np.full(n, seed & M64, np.uint64), np.full(n, (seed - P1) & M64, np.uint64)]
-        for s in range(CHUNK // 32):
+        for s in range(nw // 4):
             for k in range(4):
                 v[k] = _np_round(v[k], words[:, 4 * s + k])
         h = _np_rotl(v[0], 1) + _np_rotl(v[1], 7) + _np_rotl(v[2], 12) + _np_rotl(v[3], 18)
         for k in range(4):
             h = (h ^ _np_round(np.zeros(n, np.uint64), v[k])) * np.uint64(P1) + np.uint64(P4)
-        h = h + np.uint64(CHUNK)
+        h = h + np.uint64(8 * nw)
         h ^= h >> np.uint64(33)
         h = h * np.uint64(P2)
         h ^= h >> np.uint64(29)
@@ -107,14 +109,15 @@ def _xxh64_full_chunks(words: np.ndarray, seed: int) -> np.ndarray:
     return h
 
 
-def _level(buf: np.ndarray, seed: int) -> np.ndarray:
+def _level(buf: np.ndarray, seed: int, chunk: int = CHUNK) -> np.ndarray:
+    """XXH64 (``seed``) of every ``chunk``-byte piece of ``buf`` (the last one shorter)."""
     n = buf.size
-    full = n // CHUNK
-    out = np.zeros((n + CHUNK - 1) // CHUNK, np.uint64)
+    full = n // chunk
+    out = np.zeros((n + chunk - 1) // chunk, np.uint64)
     if full:
-        out[:full] = _xxh64_full_chunks(buf[:full * CHUNK].view("<u8").reshape(full, CHUNK // 8), seed)
-    if n % CHUNK:
-        out[full] = xxh64(buf[full * CHUNK:].tobytes(), seed)
+        out[:full] = _xxh64_full_chunks(buf[:full * chunk].view("<u8").reshape(full, chunk // 8), seed)
+    if n % chunk:
+        out[full] = xxh64(buf[full * chunk:].tobytes(), seed)
     return out
 
 
@@ -123,10 +126,11 @@ def tree_hash(data: bytes | np.ndarray, header: bytes = b"") -> int:
     buf = np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray) else \
         np.ascontiguousarray(data).reshape(-1).view(np.uint8)
     d1 = _level(buf, 1)
-    d2 = _level(d1.astype("<u8").view(np.uint8), 2) if d1.size else np.zeros(0, np.uint64)
+    d2 = _level(d1.astype("<u8").view(np.uint8), 2, 512) if d1.size else np.zeros(0, np.uint64)
+    d3 = _level(d2.astype("<u8").view(np.uint8), 3) if d2.size else np.zeros(0, np.uint64)
     hb = bytes(header)
     hw = (len(hb) + 7) // 8
     padded = np.frombuffer(hb + b"\0" * (8 * hw - len(hb)), "<u8") if hw else np.zeros(0, "<u8")
     words = np.concatenate([np.array([len(hb)], "<u8"), padded, np.array([buf.size, d1.size], "<u8"),
-                            d2.astype("<u8")])
-    return xxh64(words.tobytes(), 3)
+                            d3.astype("<u8")])
+    return xxh64(words.tobytes(), 4)

@@ -32,7 +32,7 @@ def test_library_xxh64_matches_xxhash_vectors(cuda_lib):
         assert ops.xxh64(b, seed) == d, (len(b), seed)
 
 
-@pytest.mark.parametrize("n", [0, 1, 31, 1023, 1024, 1025, 131075, 1 << 20])
+@pytest.mark.parametrize("n", [0, 1, 31, 1023, 1024, 1025, 65536, 65537, 131075, 1 << 20, 8519757])
 @pytest.mark.parametrize("hlen", [0, 3, 24, 256])
 def test_host_tree_hash_matches_oracle(cuda_lib, n, hlen):
     from vlcache_b200 import ops

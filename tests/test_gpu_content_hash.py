@@ -10,7 +10,7 @@ from oracle import content_hash as och
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n", [0, 1, 1000, 1024, 1025, 4097, 3 << 20])
+@pytest.mark.parametrize("n", [0, 1, 1000, 1024, 1025, 4097, 65537, 3 << 20, 8519757])
 def test_device_hash_matches_host_and_oracle(cuda_lib, n):
     from vlcache_b200 import ops
     rng = np.random.default_rng(n)

@@ -8,16 +8,20 @@
 // round, merge and avalanche steps, restated here) whose leaves hash in parallel:
 //
 //   level 1: d1[i] = XXH64(data[i*1024, (i+1)*1024), seed 1)        (last chunk shorter)
-//   level 2: d2[j] = XXH64(le64(d1)[j*1024, (j+1)*1024), seed 2)
+//   level 2: d2[j] = XXH64(le64(d1)[j*512, (j+1)*512), seed 2)       (64 digests a chunk)
+//   level 3: d3[k] = XXH64(le64(d2)[k*1024, (k+1)*1024), seed 3)     (128 digests a chunk)
 //   digest  = XXH64(le64 words: header_len, header zero-padded to 8 bytes, nbytes, n1,
-//                   d2[0 .. n2), seed 3)
+//                   d3[0 .. n3), seed 4)
 //
 // (n1 = number of level-1 chunks, 0 for empty data; header = the caller's bytes, e.g.
 // grid_thw, at most 256.)  The keys are used only inside one engine process, so any
 // strong 64-bit content hash keeps the reference's behaviour: same bytes, same key.
-// The GPU path: level 1 stages each block's chunks in shared memory with bulk copies and
-// hashes one chunk per thread; level 2 and the digest follow.  The host path splits level 1
-// over threads.  Both give the same digest for the same bytes.
+// The GPU path is two launches: a block of 256 threads stages 64 chunks in shared memory
+// with bulk copies, hashes each chunk with four threads (level 1) and then its 64 digests (its
+// level-2 digest: a level-2 chunk is exactly one block's digests, so level 1 never goes
+// to global memory); one block then hashes the level-2 digests (level 3) and the short
+// final stream.  The host path splits level 1 over threads.  Both give the same digest for
+// the same bytes.
 #include <algorithm>
 #include <cstring>
 #include <thread>
@@ -143,77 +147,109 @@ __host__ __device__ inline uint64_t xxh64(const uint8_t* p, int64_t len, uint64_
   return xfinish(h, p, end - p);
 }
 
-// Level 1 on the GPU: thread i hashes chunk i.  Full chunks stream 16-byte loads (the
-// four of two 32-byte stripes in flight before their rounds); the last, shorter chunk
-// (and every chunk of a buffer that is not 16-byte aligned) takes the byte-wise path.
-__global__ void __launch_bounds__(256) hash_chunks_kernel(const uint8_t* __restrict__ data, int64_t nbytes,
-                                                          uint64_t* __restrict__ out, int64_t nchunks, uint64_t seed,
-                                                          int aligned) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= nchunks) return;
-  const int64_t off = i * kChunk;
-  const int64_t len = min(kChunk, nbytes - off);
-  const uint8_t* p = data + off;
-  if (len < kChunk || !aligned) {
-    out[i] = xxh64(p, len, seed);
-    return;
+// One XXH64 of `len` bytes (at most one chunk) hashed by four consecutive threads of a warp,
+// thread `ln` running accumulator lane ln over the 64-bit words 4 s + ln of the full 32-byte
+// stripes (the four lanes of XXH64 are independent chains: split over four threads, each
+// chain has its own warp slot to hide its multiply latency).  word(i) returns the i-th
+// little-endian 64-bit word, byte(i) the i-th byte.  Every thread of the warp calls this
+// (the lanes meet through shuffles); the digest is returned in lane 0 of each group of four.
+template <typename Word, typename Byte>
+__device__ __forceinline__ uint64_t xxh64_4lanes(int64_t len, uint64_t seed, int ln, bool active, Word word,
+                                                 Byte byte) {
+  const int64_t nstripes = active ? len / 32 : 0;
+  uint64_t v = ln == 0 ? seed + P1 + P2 : ln == 1 ? seed + P2 : ln == 2 ? seed : seed - P1;
+#pragma unroll 8
+  for (int64_t s = 0; s < nstripes; ++s) v = xround(v, word(4 * s + ln));
+  const unsigned full = 0xffffffffu;
+  const uint64_t v2 = __shfl_down_sync(full, v, 1), v3 = __shfl_down_sync(full, v, 2),
+                 v4 = __shfl_down_sync(full, v, 3);
+  if (!active || ln != 0) return 0;
+  uint64_t h = (len >= 32 ? xstripes_done(v, v2, v3, v4) : seed + P5) + (uint64_t)len;
+  // the tail (fewer than 32 bytes) and the final mix, as xfinish does
+  int64_t i = nstripes * 32;
+  for (; i + 8 <= len; i += 8) {
+    h ^= xround(0, word(i / 8));
+    h = rotl64(h, 27) * P1 + P4;
   }
-  uint64_t v1 = seed + P1 + P2, v2 = seed + P2, v3 = seed, v4 = seed - P1;
-  const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll 4
-  for (int s = 0; s < kChunk / 64; ++s) {
-    const uint4 a = __ldg(q + 4 * s), b = __ldg(q + 4 * s + 1), c = __ldg(q + 4 * s + 2), d = __ldg(q + 4 * s + 3);
-    v1 = xround(v1, ((uint64_t)a.y << 32) | a.x);
-    v2 = xround(v2, ((uint64_t)a.w << 32) | a.z);
-    v3 = xround(v3, ((uint64_t)b.y << 32) | b.x);
-    v4 = xround(v4, ((uint64_t)b.w << 32) | b.z);
-    v1 = xround(v1, ((uint64_t)c.y << 32) | c.x);
-    v2 = xround(v2, ((uint64_t)c.w << 32) | c.z);
-    v3 = xround(v3, ((uint64_t)d.y << 32) | d.x);
-    v4 = xround(v4, ((uint64_t)d.w << 32) | d.z);
+  if (i + 4 <= len) {
+    const uint32_t w4 = (uint32_t)byte(i) | ((uint32_t)byte(i + 1) << 8) | ((uint32_t)byte(i + 2) << 16) |
+                        ((uint32_t)byte(i + 3) << 24);
+    h ^= (uint64_t)w4 * P1;
+    h = rotl64(h, 23) * P2 + P3;
+    i += 4;
   }
-  const uint64_t h = xstripes_done(v1, v2, v3, v4) + (uint64_t)kChunk;
-  out[i] = avalanche(h);  // a full chunk leaves no tail
+  for (; i < len; ++i) {
+    h ^= (uint64_t)byte(i) * P5;
+    h = rotl64(h, 11) * P1;
+  }
+  return avalanche(h);
 }
 
-// Level 1, staged: a block's 64 full chunks come into shared memory with one 1 KB bulk copy
-// each (the copy engine streams whole chunks; a lane-per-chunk global read would touch 32
-// lines per warp access), rows padded to 1,040 bytes so that the 8 lanes of a 16-byte
-// shared-memory access hit distinct banks; then thread i hashes chunk i from shared memory.
-// The waits are bounded (a timeout records a device error and the block returns).
-constexpr int kStageChunks = 64;
+// Levels 1 and 2 on the GPU: block b hashes chunks [64 b, 64 b + 64), four threads a chunk
+// (xxh64_4lanes), and then their 64 digests, d2[b].  kStaged (16-byte aligned data): the
+// block's full chunks are brought into shared memory with one 1 KB bulk copy each (the copy
+// engine streams whole chunks), rows padded to 1,040 bytes so that a warp's 8-byte reads (8
+// chunks x 4 lanes) spread over the banks; the shorter last chunk is copied in by the
+// block's threads.  Unaligned data is read from global memory.  The wait is bounded (a
+// timeout records a device error and the block returns, leaving its digest unwritten).
+constexpr int kStageChunks = 64;              // level-1 chunks per block = digests per level-2 chunk
+constexpr int kLevel1Threads = 4 * kStageChunks;
+constexpr int kL3Group = 128;                 // level-2 digests per level-3 chunk
 constexpr int kStageRow = kChunk + 16;
-constexpr int kStageSmem = kStageChunks * kStageRow + 64;
-__global__ void __launch_bounds__(kStageChunks) hash_chunks_staged_kernel(const uint8_t* __restrict__ data,
-                                                                          uint64_t* __restrict__ out,
-                                                                          int64_t full_chunks, uint64_t seed) {
+constexpr int kStageSmem = kStageChunks * kStageRow + kStageChunks * 8 + 64;
+constexpr int kPlainSmem = kStageChunks * 8 + 64;
+template <bool kStaged>
+__global__ void __launch_bounds__(kLevel1Threads, 3) hash_level12_kernel(const uint8_t* __restrict__ data,
+                                                                         int64_t nbytes,
+                                                                         uint64_t* __restrict__ d2) {
   extern __shared__ __align__(128) uint8_t stage[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(stage + kStageChunks * kStageRow);
+  uint64_t* dig = reinterpret_cast<uint64_t*>(stage + (kStaged ? kStageChunks * kStageRow : 0));
+  uint64_t* bar = dig + kStageChunks;
+  const int64_t n1 = (nbytes + kChunk - 1) / kChunk, full = nbytes / kChunk;
   const int64_t c0 = (int64_t)blockIdx.x * kStageChunks;
-  const int n = (int)min((int64_t)kStageChunks, full_chunks - c0);
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
+  const int nb = (int)min((int64_t)kStageChunks, n1 - c0);                    // chunks of this block
+  const int t = threadIdx.x, ci = t >> 2, ln = t & 3;
+  if (kStaged) {
+    const int nfull = (int)max((int64_t)0, min((int64_t)nb, full - c0));
+    if (t == 0) {
+      mbar_init(bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (t == 0 && nfull > 0) {
+      mbar_expect_tx(bar, (uint32_t)(nfull * kChunk));
+      for (int c = 0; c < nfull; ++c) bulk_load_1d(stage + c * kStageRow, data + (c0 + c) * kChunk, kChunk, bar);
+    }
+    if (nb > nfull && t < kChunk / 16) {
+      // the shorter last chunk (only the last block has one): 16 bytes a thread, the bytes
+      // past nbytes one at a time
+      const int64_t off = (c0 + nfull) * kChunk;
+      const int rem = (int)(nbytes - off), b0 = 16 * t;
+      uint8_t* row = stage + nfull * kStageRow;
+      if (b0 + 16 <= rem)
+        *reinterpret_cast<uint4*>(row + b0) = *reinterpret_cast<const uint4*>(data + off + b0);
+      else
+        for (int bb = b0; bb < rem; ++bb) row[bb] = data[off + bb];
+    }
+    const bool ok = nfull == 0 || mbar_wait_bounded(bar, 0, VLC_DEV_ERR_TIMEOUT + 50, VLC_WAIT_LIMIT_CYCLES);
+    if (!__syncthreads_and(ok)) return;  // every thread leaves together (and the last chunk is in place)
   }
+  const int64_t off = (c0 + ci) * kChunk;
+  const int64_t len = ci < nb ? min(kChunk, nbytes - off) : 0;
+  uint64_t h;
+  if (kStaged) {
+    const uint8_t* row = stage + ci * kStageRow;
+    h = xxh64_4lanes(
+        len, 1, ln, ci < nb, [&](int64_t i) { return reinterpret_cast<const uint64_t*>(row)[i]; },
+        [&](int64_t i) { return row[i]; });
+  } else {
+    const uint8_t* src = data + off;
+    h = xxh64_4lanes(
+        len, 1, ln, ci < nb, [&](int64_t i) { return rd64(src + 8 * i); }, [&](int64_t i) { return src[i]; });
+  }
+  if (ln == 0 && ci < nb) dig[ci] = h;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_expect_tx(bar, (uint32_t)(n * kChunk));
-    for (int i = 0; i < n; ++i) bulk_load_1d(stage + i * kStageRow, data + (c0 + i) * kChunk, kChunk, bar);
-  }
-  if (!mbar_wait_bounded(bar, 0, VLC_DEV_ERR_TIMEOUT + 50, VLC_WAIT_LIMIT_CYCLES)) return;
-  const int i = threadIdx.x;
-  if (i >= n) return;
-  uint64_t v1 = seed + P1 + P2, v2 = seed + P2, v3 = seed, v4 = seed - P1;
-  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(stage + i * kStageRow);
-#pragma unroll 8
-  for (int s = 0; s < kChunk / 32; ++s) {
-    const ulonglong2 a = q[2 * s], b = q[2 * s + 1];
-    v1 = xround(v1, a.x);
-    v2 = xround(v2, a.y);
-    v3 = xround(v3, b.x);
-    v4 = xround(v4, b.y);
-  }
-  out[c0 + i] = avalanche(xstripes_done(v1, v2, v3, v4) + (uint64_t)kChunk);
+  if (t == 0) d2[blockIdx.x] = xxh64_words(dig, nb, 2);
 }
 
 struct Header {
@@ -221,42 +257,47 @@ struct Header {
   int len;
 };
 
-// Level 2: thread j hashes level-2 chunk j, i.e. 128 level-1 digests (fewer in the
-// last), as 64-bit words with 16-byte loads: XXH64 of 8k bytes is xxh64_words of k words.
-__global__ void __launch_bounds__(256) hash_level2_kernel(const uint64_t* __restrict__ d1, int64_t n1,
-                                                          uint64_t* __restrict__ d2, int64_t n2) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= n2) return;
-  const int64_t w0 = j * (kChunk / 8);
-  const int64_t cnt = min((int64_t)(kChunk / 8), n1 - w0);
-  if (cnt < kChunk / 8) {
-    d2[j] = xxh64_words(d1 + w0, cnt, 2);
-    return;
-  }
-  uint64_t v1 = 2 + P1 + P2, v2 = 2 + P2, v3 = 2, v4 = 2 - P1;
-  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(d1 + w0);
-#pragma unroll 4
-  for (int s = 0; s < kChunk / 32; ++s) {
-    const ulonglong2 a = q[2 * s], b = q[2 * s + 1];
-    v1 = xround(v1, a.x);
-    v2 = xround(v2, a.y);
-    v3 = xround(v3, b.x);
-    v4 = xround(v4, b.y);
-  }
-  d2[j] = avalanche(xstripes_done(v1, v2, v3, v4) + (uint64_t)kChunk);
-}
-
-// The digest, one block: the final word stream is gathered in shared memory (the level-2
-// digests copied by all threads), then thread 0 hashes it.
+// Level 3 and the digest, one block: the level-2 digests come into shared memory in
+// windows of kFinalWindow words (coalesced, eight loads in flight per thread), four threads
+// hash each level-3 chunk of the window (128 level-2 digests, fewer in the last) into the
+// final word stream, also in shared memory, and thread 0 hashes that stream.
 constexpr int kFinalThreads = 256;
+constexpr int kFinalWindow = kFinalThreads / 4 * kL3Group;  // words: 64 KB, one level-3 chunk per 4 threads
 constexpr int kFinalSmemMax = 200 * 1024;
 __global__ void __launch_bounds__(kFinalThreads) hash_final_kernel(const uint64_t* __restrict__ d2, int64_t n2,
                                                                    int64_t n1, int64_t nbytes,
                                                                    const __grid_constant__ Header hdr, uint64_t* out) {
-  extern __shared__ uint64_t words[];  // [1 + header words + 2 + n2]
+  extern __shared__ uint64_t smem_words[];  // [window][1 + header words + 2 + n3]
+  uint64_t* win = smem_words;
+  uint64_t* words = smem_words + kFinalWindow;
   const int hw = (hdr.len + 7) / 8;
-  for (int64_t j = threadIdx.x; j < n2; j += blockDim.x) words[3 + hw + j] = d2[j];
-  if (threadIdx.x == 0) {
+  const int t = threadIdx.x, ck = t >> 2, ln = t & 3;
+  for (int64_t w0 = 0; w0 < n2; w0 += kFinalWindow) {
+    const int64_t cnt = min((int64_t)kFinalWindow, n2 - w0);
+    __syncthreads();  // the previous window is hashed
+    for (int64_t j0 = 0; j0 < cnt; j0 += 8 * kFinalThreads) {
+      uint64_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t j = j0 + u * kFinalThreads + t;
+        v[u] = j < cnt ? d2[w0 + j] : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t j = j0 + u * kFinalThreads + t;
+        if (j < cnt) win[j] = v[u];
+      }
+    }
+    __syncthreads();
+    const int64_t k = (int64_t)ck;  // level-3 chunk of this window
+    const int64_t nw = max((int64_t)0, min((int64_t)kL3Group, cnt - k * kL3Group));
+    const uint64_t* cw = win + k * kL3Group;
+    const uint64_t h = xxh64_4lanes(
+        8 * nw, 3, ln, nw > 0, [&](int64_t i) { return cw[i]; },
+        [&](int64_t i) { return (uint8_t)(cw[i >> 3] >> (8 * (i & 7))); });
+    if (ln == 0 && nw > 0) words[3 + hw + w0 / kL3Group + k] = h;
+  }
+  if (t == 0) {
     words[0] = (uint64_t)hdr.len;
     for (int k = 0; k < hw; ++k) {
       uint64_t v = 0;
@@ -267,27 +308,29 @@ __global__ void __launch_bounds__(kFinalThreads) hash_final_kernel(const uint64_
     words[2 + hw] = (uint64_t)n1;
   }
   __syncthreads();
-  if (threadIdx.x == 0) *out = xxh64_words(words, 3 + hw + n2, 3);
+  if (threadIdx.x == 0) *out = xxh64_words(words, 3 + hw + (n2 + kL3Group - 1) / kL3Group, 4);
 }
 
 inline int64_t level1_chunks(int64_t nbytes) { return (nbytes + kChunk - 1) / kChunk; }
-inline int64_t level2_chunks(int64_t n1) { return (n1 * 8 + kChunk - 1) / kChunk; }
+inline int64_t level2_chunks(int64_t n1) { return (n1 + kStageChunks - 1) / kStageChunks; }
+inline int64_t level3_chunks(int64_t n2) { return (n2 + kL3Group - 1) / kL3Group; }
 
-// Host digest from the level-1 digests (the same steps as hash_final_kernel).
+// Host digest from the level-1 digests (the same steps as the device kernels).
 uint64_t host_final(const std::vector<uint64_t>& d1, int64_t nbytes, const uint8_t* header, int header_len) {
   const int64_t n1 = (int64_t)d1.size();
-  const int64_t bytes1 = n1 * 8;
-  const int64_t n2 = level2_chunks(n1);
+  const int64_t n2 = level2_chunks(n1), n3 = level3_chunks(n2);
+  std::vector<uint64_t> d2((size_t)n2);
+  for (int64_t j = 0; j < n2; ++j)
+    d2[(size_t)j] = xxh64_words(d1.data() + j * kStageChunks, std::min<int64_t>(kStageChunks, n1 - j * kStageChunks), 2);
   const int hw = (header_len + 7) / 8;
-  std::vector<uint64_t> w((size_t)(3 + hw + n2), 0);
+  std::vector<uint64_t> w((size_t)(3 + hw + n3), 0);
   w[0] = (uint64_t)header_len;
   for (int b = 0; b < header_len; ++b) w[1 + b / 8] |= (uint64_t)header[b] << (8 * (b % 8));
   w[1 + hw] = (uint64_t)nbytes;
   w[2 + hw] = (uint64_t)n1;
-  const uint8_t* b1 = reinterpret_cast<const uint8_t*>(d1.data());
-  for (int64_t j = 0; j < n2; ++j)
-    w[(size_t)(3 + hw + j)] = xxh64(b1 + j * kChunk, std::min(kChunk, bytes1 - j * kChunk), 2);
-  return xxh64_words(w.data(), (int64_t)w.size(), 3);
+  for (int64_t k = 0; k < n3; ++k)
+    w[(size_t)(3 + hw + k)] = xxh64_words(d2.data() + k * kL3Group, std::min<int64_t>(kL3Group, n2 - k * kL3Group), 3);
+  return xxh64_words(w.data(), (int64_t)w.size(), 4);
 }
 
 }  // namespace chash
@@ -298,8 +341,7 @@ using namespace vlc::chash;
 
 extern "C" int64_t vlc_content_hash_workspace_size(int64_t nbytes) {
   if (nbytes < 0) return -1;
-  const int64_t n1 = level1_chunks(nbytes);
-  return std::max<int64_t>(1, n1 + level2_chunks(n1)) * 8;  // the level-1 and level-2 digests
+  return std::max<int64_t>(1, level2_chunks(level1_chunks(nbytes))) * 8;  // the level-2 digests
 }
 
 extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const void* header, int header_bytes,
@@ -311,39 +353,20 @@ extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const v
   if ((uintptr_t)workspace % 16 != 0 || (uintptr_t)digest % 8 != 0) return VLC_ERR_ALIGN;
   const int64_t n1 = level1_chunks(nbytes);
   const int64_t n2 = level2_chunks(n1);
-  const int64_t final_smem = (3 + (header_bytes + 7) / 8 + n2) * 8;
-  if (final_smem > kFinalSmemMax) return VLC_ERR_UNSUPPORTED;  // inputs above about 3 TB
-  uint64_t* d1 = (uint64_t*)workspace;
-  uint64_t* d2 = d1 + n1;  // 16-byte aligned chunks of d1 (1,024 bytes each)
+  const int64_t final_smem = (kFinalWindow + 3 + (header_bytes + 7) / 8 + level3_chunks(n2)) * 8;
+  if (final_smem > kFinalSmemMax || n2 > 0x7fffffff) return VLC_ERR_UNSUPPORTED;  // inputs above about 100 GB
+  uint64_t* d2 = (uint64_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
   if (n1 > 0) {
-    const int64_t blocks = (n1 + 255) / 256;
-    if (blocks > 0x7fffffff) return VLC_ERR_SHAPE;
-    int rc;
-    const int64_t full = nbytes / kChunk;
-    if (aligned16(data) && full > 0) {
-      // full chunks staged through shared memory; the shorter last chunk on its own
+    if (aligned16(data)) {
       static std::atomic<uint64_t> staged_set{0};
-      if (ensure_dynamic_smem((const void*)hash_chunks_staged_kernel, kStageSmem, staged_set) != VLC_OK)
+      if (ensure_dynamic_smem((const void*)hash_level12_kernel<true>, kStageSmem, staged_set) != VLC_OK)
         return VLC_ERR_CUDA;
-      hash_chunks_staged_kernel<<<(unsigned)((full + kStageChunks - 1) / kStageChunks), kStageChunks, kStageSmem,
-                                  st>>>((const uint8_t*)data, d1, full, 1);
-      rc = launch_status();
-      if (rc != VLC_OK) return rc;
-      if (full < n1) {
-        hash_chunks_kernel<<<1, 32, 0, st>>>((const uint8_t*)data + full * kChunk, nbytes - full * kChunk,
-                                             d1 + full, 1, 1, 0);
-        rc = launch_status();
-        if (rc != VLC_OK) return rc;
-      }
+      hash_level12_kernel<true><<<(unsigned)n2, kLevel1Threads, kStageSmem, st>>>((const uint8_t*)data, nbytes, d2);
     } else {
-      hash_chunks_kernel<<<(unsigned)blocks, 256, 0, st>>>((const uint8_t*)data, nbytes, d1, n1, 1,
-                                                           aligned16(data) ? 1 : 0);
-      rc = launch_status();
-      if (rc != VLC_OK) return rc;
+      hash_level12_kernel<false><<<(unsigned)n2, kLevel1Threads, kPlainSmem, st>>>((const uint8_t*)data, nbytes, d2);
     }
-    hash_level2_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(d1, n1, d2, n2);
-    rc = launch_status();
+    const int rc = launch_status();
     if (rc != VLC_OK) return rc;
   }
   Header h;
