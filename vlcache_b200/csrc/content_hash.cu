@@ -17,7 +17,7 @@
 // grid_thw, at most 256.)  The keys are used only inside one engine process, so any
 // strong 64-bit content hash keeps the reference's behaviour: same bytes, same key.
 // The GPU path is two launches: a block of 256 threads stages 64 chunks in shared memory
-// with bulk copies, hashes each chunk with four threads (level 1) and then its 64 digests (its
+// with TMA loads, hashes each chunk with four threads (level 1) and then its 64 digests (its
 // level-2 digest: a level-2 chunk is exactly one block's digests, so level 1 never goes
 // to global memory); one block then hashes the level-2 digests (level 3) and the short
 // final stream.  The host path splits level 1 over threads.  Both give the same digest for
@@ -153,17 +153,21 @@ __host__ __device__ inline uint64_t xxh64(const uint8_t* p, int64_t len, uint64_
 // chain has its own warp slot to hide its multiply latency).  word(i) returns the i-th
 // little-endian 64-bit word, byte(i) the i-th byte.  Every thread of the warp calls this
 // (the lanes meet through shuffles); the digest is returned in lane 0 of each group of four.
+__device__ __forceinline__ uint64_t lane_init(uint64_t seed, int ln) {
+  return ln == 0 ? seed + P1 + P2 : ln == 1 ? seed + P2 : ln == 2 ? seed : seed - P1;
+}
+
+// The end of xxh64_4lanes: every thread of the warp passes its lane's accumulator v (after
+// the len / 32 full stripes); lane 0 of each group of four merges the four, hashes the
+// tail and returns the digest (the others return 0).
 template <typename Word, typename Byte>
-__device__ __forceinline__ uint64_t xxh64_4lanes(int64_t len, uint64_t seed, int ln, bool active, Word word,
-                                                 Byte byte) {
-  const int64_t nstripes = active ? len / 32 : 0;
-  uint64_t v = ln == 0 ? seed + P1 + P2 : ln == 1 ? seed + P2 : ln == 2 ? seed : seed - P1;
-#pragma unroll 8
-  for (int64_t s = 0; s < nstripes; ++s) v = xround(v, word(4 * s + ln));
+__device__ __forceinline__ uint64_t xxh64_4lanes_finish(uint64_t v, int64_t len, uint64_t seed, int ln, bool active,
+                                                        Word word, Byte byte) {
   const unsigned full = 0xffffffffu;
   const uint64_t v2 = __shfl_down_sync(full, v, 1), v3 = __shfl_down_sync(full, v, 2),
                  v4 = __shfl_down_sync(full, v, 3);
   if (!active || ln != 0) return 0;
+  const int64_t nstripes = len / 32;
   uint64_t h = (len >= 32 ? xstripes_done(v, v2, v3, v4) : seed + P5) + (uint64_t)len;
   // the tail (fewer than 32 bytes) and the final mix, as xfinish does
   int64_t i = nstripes * 32;
@@ -185,63 +189,116 @@ __device__ __forceinline__ uint64_t xxh64_4lanes(int64_t len, uint64_t seed, int
   return avalanche(h);
 }
 
+template <typename Word, typename Byte>
+__device__ __forceinline__ uint64_t xxh64_4lanes(int64_t len, uint64_t seed, int ln, bool active, Word word,
+                                                 Byte byte) {
+  const int64_t nstripes = active ? len / 32 : 0;
+  uint64_t v = lane_init(seed, ln);
+#pragma unroll 8
+  for (int64_t s = 0; s < nstripes; ++s) v = xround(v, word(4 * s + ln));
+  return xxh64_4lanes_finish(v, len, seed, ln, active, word, byte);
+}
+
 // Levels 1 and 2 on the GPU: block b hashes chunks [64 b, 64 b + 64), four threads a chunk
 // (xxh64_4lanes), and then their 64 digests, d2[b].  kStaged (16-byte aligned data): the
-// block's full chunks are brought into shared memory with one 1 KB bulk copy each (the copy
-// engine streams whole chunks), rows padded to 1,040 bytes so that a warp's 8-byte reads (8
-// chunks x 4 lanes) spread over the banks; the shorter last chunk is copied in by the
-// block's threads.  Unaligned data is read from global memory.  The wait is bounded (a
-// timeout records a device error and the block returns, leaving its digest unwritten).
+// block's full chunks come into shared memory by 8 TMA tensor loads over the chunks viewed
+// as a 2-D tensor [chunks][1,024 bytes]: load b is the 128-byte column slab b of all 64
+// chunks (8 KB, 128-byte swizzle: 16-byte unit u of chunk c at unit u ^ (c & 7)), so a
+// warp's 8-byte reads (8 chunks x 4 lanes) hit every bank evenly; the shorter last chunk
+// (past the tensor's rows, which the loads fill with zeros) is copied by the block's
+// threads into a buffer of its own.  Unaligned data is read from global memory.  The wait
+// is bounded (a timeout records a device error and the block returns, leaving its digest
+// unwritten).
 constexpr int kStageChunks = 64;              // level-1 chunks per block = digests per level-2 chunk
 constexpr int kLevel1Threads = 4 * kStageChunks;
 constexpr int kL3Group = 128;                 // level-2 digests per level-3 chunk
-constexpr int kStageRow = kChunk + 16;
-constexpr int kStageSmem = kStageChunks * kStageRow + kStageChunks * 8 + 64;
+constexpr int kSlabBytes = kStageChunks * 128;  // one 128-byte column of every chunk: 8 KB
+constexpr int kSlabs = kChunk / 128;
+constexpr int kOffTail = kSlabs * kSlabBytes;   // the shorter last chunk
+constexpr int kOffDig = kOffTail + kChunk;      // the block's level-1 digests
+constexpr int kOffBar = kOffDig + kStageChunks * 8;
+constexpr int kStageSmem = kOffBar + 64 + 1024;  // + alignment of the swizzled slabs to 1,024 bytes
 constexpr int kPlainSmem = kStageChunks * 8 + 64;
 template <bool kStaged>
-__global__ void __launch_bounds__(kLevel1Threads, 3) hash_level12_kernel(const uint8_t* __restrict__ data,
+__global__ void __launch_bounds__(kLevel1Threads, 3) hash_level12_kernel(const __grid_constant__ CUtensorMap tm,
+                                                                         const uint8_t* __restrict__ data,
                                                                          int64_t nbytes,
                                                                          uint64_t* __restrict__ d2) {
-  extern __shared__ __align__(128) uint8_t stage[];
-  uint64_t* dig = reinterpret_cast<uint64_t*>(stage + (kStaged ? kStageChunks * kStageRow : 0));
-  uint64_t* bar = dig + kStageChunks;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* sm = kStaged ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023))
+                        : smem_raw;
+  uint64_t* dig = reinterpret_cast<uint64_t*>(sm + (kStaged ? kOffDig : 0));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + (kStaged ? kOffBar : kStageChunks * 8));
   const int64_t n1 = (nbytes + kChunk - 1) / kChunk, full = nbytes / kChunk;
   const int64_t c0 = (int64_t)blockIdx.x * kStageChunks;
   const int nb = (int)min((int64_t)kStageChunks, n1 - c0);                    // chunks of this block
   const int t = threadIdx.x, ci = t >> 2, ln = t & 3;
+  int nfull = 0;
   if (kStaged) {
-    const int nfull = (int)max((int64_t)0, min((int64_t)nb, full - c0));
+    nfull = (int)max((int64_t)0, min((int64_t)nb, full - c0));
     if (t == 0) {
       mbar_init(bar, 1);
       fence_mbar_init();
     }
     __syncthreads();
     if (t == 0 && nfull > 0) {
-      mbar_expect_tx(bar, (uint32_t)(nfull * kChunk));
-      for (int c = 0; c < nfull; ++c) bulk_load_1d(stage + c * kStageRow, data + (c0 + c) * kChunk, kChunk, bar);
+      mbar_expect_tx(bar, (uint32_t)(kSlabs * kSlabBytes));  // whole boxes (rows past the tensor: zeros)
+      for (int sb = 0; sb < kSlabs; ++sb) tma_load_2d(sm + sb * kSlabBytes, &tm, bar, sb * 64, (int)c0);
     }
     if (nb > nfull && t < kChunk / 16) {
       // the shorter last chunk (only the last block has one): 16 bytes a thread, the bytes
       // past nbytes one at a time
       const int64_t off = (c0 + nfull) * kChunk;
       const int rem = (int)(nbytes - off), b0 = 16 * t;
-      uint8_t* row = stage + nfull * kStageRow;
+      uint8_t* tail = sm + kOffTail;
       if (b0 + 16 <= rem)
-        *reinterpret_cast<uint4*>(row + b0) = *reinterpret_cast<const uint4*>(data + off + b0);
+        *reinterpret_cast<uint4*>(tail + b0) = *reinterpret_cast<const uint4*>(data + off + b0);
       else
-        for (int bb = b0; bb < rem; ++bb) row[bb] = data[off + bb];
+        for (int bb = b0; bb < rem; ++bb) tail[bb] = data[off + bb];
     }
-    const bool ok = nfull == 0 || mbar_wait_bounded(bar, 0, VLC_DEV_ERR_TIMEOUT + 50, VLC_WAIT_LIMIT_CYCLES);
+    // Warp 0 polls the loads' barrier (sleeping between polls, so that the hashing warps of
+    // the SM's other blocks keep its issue slots); the other warps wait at the block barrier,
+    // which also carries warp 0's observation of the loaded bytes to them.
+    bool ok = true;
+    if (t < 32 && nfull > 0) {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(bar, 0)) {
+        if (clock64() - t0 > VLC_WAIT_LIMIT_CYCLES) {
+          if (t == 0) record_error(VLC_DEV_ERR_TIMEOUT + 50);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
     if (!__syncthreads_and(ok)) return;  // every thread leaves together (and the last chunk is in place)
   }
   const int64_t off = (c0 + ci) * kChunk;
   const int64_t len = ci < nb ? min(kChunk, nbytes - off) : 0;
   uint64_t h;
   if (kStaged) {
-    const uint8_t* row = stage + ci * kStageRow;
-    h = xxh64_4lanes(
-        len, 1, ln, ci < nb, [&](int64_t i) { return reinterpret_cast<const uint64_t*>(row)[i]; },
-        [&](int64_t i) { return row[i]; });
+    // A full chunk in the slabs: lane ln's words 4 s + ln are bytes 32 s + 8 ln, i.e. slab
+    // s / 4, 16-byte unit 2 (s % 4) + ln / 2 (swizzled by the chunk's row), half ln % 2: four
+    // offsets per thread, one add per word.  The shorter last chunk: from its own buffer.
+    const uint8_t* tail = sm + kOffTail;
+    uint64_t v = lane_init(1, ln);
+    if (ci < nfull) {
+      const uint8_t* row = sm + ci * 128 + 8 * (ln & 1);
+      const int sw = ci & 7;
+      int offj[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) offj[j] = ((2 * j + (ln >> 1)) ^ sw) * 16;
+#pragma unroll
+      for (int g = 0; g < kSlabs; ++g)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v = xround(v, *reinterpret_cast<const uint64_t*>(row + g * kSlabBytes + offj[j]));
+    } else if (ci < nb) {
+      const uint64_t* tw = reinterpret_cast<const uint64_t*>(tail);
+      for (int64_t s2 = 0; s2 < len / 32; ++s2) v = xround(v, tw[4 * s2 + ln]);
+    }
+    h = xxh64_4lanes_finish(
+        v, len, 1, ln, ci < nb, [&](int64_t i) { return reinterpret_cast<const uint64_t*>(tail)[i]; },
+        [&](int64_t i) { return tail[i]; });  // the tail bytes: only the shorter chunk has them
   } else {
     const uint8_t* src = data + off;
     h = xxh64_4lanes(
@@ -358,13 +415,23 @@ extern "C" int vlc_content_hash_device(const void* data, int64_t nbytes, const v
   uint64_t* d2 = (uint64_t*)workspace;
   cudaStream_t st = (cudaStream_t)stream;
   if (n1 > 0) {
-    if (aligned16(data)) {
+    const int64_t full = nbytes / kChunk;
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof(tm));
+    if (aligned16(data) && full > 0) {
+      // the full chunks as a 2-D tensor [full][512 two-byte elements], boxes {64, 64}
+      const uint64_t dims[2] = {(uint64_t)(kChunk / 2), (uint64_t)full};
+      const uint64_t strides[1] = {(uint64_t)kChunk};
+      const uint32_t box[2] = {64, (uint32_t)kStageChunks};
+      if (encode_tmap_bf16(&tm, data, 2, dims, strides, box, 128) != VLC_OK) return VLC_ERR_CUDA;
       static std::atomic<uint64_t> staged_set{0};
       if (ensure_dynamic_smem((const void*)hash_level12_kernel<true>, kStageSmem, staged_set) != VLC_OK)
         return VLC_ERR_CUDA;
-      hash_level12_kernel<true><<<(unsigned)n2, kLevel1Threads, kStageSmem, st>>>((const uint8_t*)data, nbytes, d2);
+      hash_level12_kernel<true><<<(unsigned)n2, kLevel1Threads, kStageSmem, st>>>(tm, (const uint8_t*)data, nbytes,
+                                                                                  d2);
     } else {
-      hash_level12_kernel<false><<<(unsigned)n2, kLevel1Threads, kPlainSmem, st>>>((const uint8_t*)data, nbytes, d2);
+      hash_level12_kernel<false><<<(unsigned)n2, kLevel1Threads, kPlainSmem, st>>>(tm, (const uint8_t*)data, nbytes,
+                                                                                   d2);
     }
     const int rc = launch_status();
     if (rc != VLC_OK) return rc;
