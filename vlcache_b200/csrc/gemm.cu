@@ -58,7 +58,7 @@ struct Tile {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (225 * 1024) / STAGE_BYTES < 6 ? (225 * 1024) / STAGE_BYTES : 6;
   static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-  static constexpr int NUM_BARS = 2 * STAGES + 4;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int NUM_BARS = 2 * STAGES + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], fix_full
   static constexpr int OFF_MISC = (OFF_BAR + NUM_BARS * 8 + 127) / 128 * 128;
   static constexpr int OFF_BIAS = OFF_MISC + 64;   // each epilogue warp's copy of the tile's bias
   static constexpr int SMEM_BYTES = OFF_BIAS + 4 * 256 * 2 + 1024;
@@ -270,7 +270,35 @@ __device__ __forceinline__ int sk_slot(const Params& p, int c, int t) {
 struct Fixup {
   int c_lo, c_hi;  // CTAs covering the tile (none when c_lo > c_hi)
   int t;
+  // The other CTAs' partials staged in this CTA's free operand ring, one 128-column half at a
+  // time (stage_parts), or null: read from L2 (global memory).  Partial j (the j-th other CTA
+  // in CTA order) at float4 j * 4096, in the workspace's own layout.
+  const float4* stage;
+  uint64_t* bar;  // completes once per staged half
+  bool leader;    // issues the bulk copies
 };
+
+// Stage column half h (chunks [4 h, 4 h + 4): 64 KB of each partial, contiguous in the
+// workspace) of the tile's other partials into the ring.  Every epilogue thread calls it:
+// the named barrier keeps the previous half's readers ahead of the copies that overwrite it.
+__device__ __forceinline__ void stage_parts(const Params& p, const Fixup& fx, int h) {
+  named_bar_sync(1, 128);
+  if (fx.leader) {
+    // the partials (global) and the previous half's shared-memory reads, before the copy
+    // engine reads the one and overwrites the other
+    asm volatile("fence.proxy.async;" ::: "memory");
+    mbar_expect_tx(fx.bar, (uint32_t)(fx.c_hi - fx.c_lo) * 65536u);
+    int j = 0;
+    for (int c = fx.c_lo; c <= fx.c_hi; ++c) {
+      if (c == (int)blockIdx.x) continue;
+      const float4* src = reinterpret_cast<const float4*>(p.partials) + (int64_t)sk_slot(p, c, fx.t) * (BM * BN / 4) +
+                          (int64_t)h * 32 * BM;
+      bulk_load_1d(const_cast<float4*>(fx.stage) + j * 4096, src, 65536u, fx.bar);
+      ++j;
+    }
+  }
+  mbar_wait_bounded(fx.bar, (uint32_t)h, VLC_DEV_ERR_TIMEOUT + 51, VLC_WAIT_LIMIT_CYCLES);
+}
 
 template <int TN>
 __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, const Fixup& fx, int r_in, int col,
@@ -291,11 +319,14 @@ __device__ __forceinline__ void load_acc32(const Params& p, uint32_t taddr, cons
       for (int i = 0; i < 32; ++i) v[i] += __uint_as_float(raw[i]);
       continue;
     }
-    const float4* src = reinterpret_cast<const float4*>(p.partials) +
-                        (int64_t)sk_slot(p, c, fx.t) * (BM * TN / 4) + (col / 4) * BM + r_in;
+    const int j = c - fx.c_lo - (c > (int)blockIdx.x ? 1 : 0);  // among the other CTAs
+    const float4* src = fx.stage != nullptr ? fx.stage + j * 4096 + ((col & 127) / 4) * BM + r_in
+                                            : reinterpret_cast<const float4*>(p.partials) +
+                                                  (int64_t)sk_slot(p, c, fx.t) * (BM * TN / 4) + (col / 4) * BM + r_in;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 f = __ldcg(src + i * BM);
+      // staged: a shared-memory load (ld.global.cg takes global addresses only)
+      const float4 f = fx.stage != nullptr ? src[i * BM] : __ldcg(src + i * BM);
       v[4 * i] += f.x;
       v[4 * i + 1] += f.y;
       v[4 * i + 2] += f.z;
@@ -316,6 +347,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
     const int n0 = nt * TN;
 #pragma unroll 1
     for (int c = 0; c < TN / 32; ++c) {
+      if (fx.stage != nullptr && c % 4 == 0) stage_parts(p, fx, c / 4);
       float v[32];
       load_acc32<TN>(p, tacc + c * 32, fx, r_in, c * 32, v);
       const int col = n0 + c * 32;
@@ -466,6 +498,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
   uint64_t* empty = full + TL::STAGES;
   uint64_t* acc_full = full + 2 * TL::STAGES;
   uint64_t* acc_empty = acc_full + 2;
+  uint64_t* fix_full = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TL::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TL::OFF_MISC + 4);
   volatile int* ticket_last = reinterpret_cast<volatile int*>(smem + TL::OFF_MISC + 8);
@@ -485,6 +518,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       mbar_init(acc_full + b, 1);
       mbar_init(acc_empty + b, 128);
     }
+    mbar_init(fix_full, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -589,6 +623,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       fx.t = t;
       fx.c_lo = 1;
       fx.c_hi = 0;  // no partials to add
+      fx.stage = nullptr;
+      fx.bar = fix_full;
+      fx.leader = leader;
       if (EPI != kQkvRope && (sg.kb_lo != 0 || sg.kb_hi != p.k_blocks)) {
         // Stream-K: this CTA covers part of the tile.  Leave the partial, take a ticket.
         // Partial layout: 16-byte piece q (columns 4q .. 4q + 3) of row r at float4 index
@@ -627,6 +664,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
         }
         fx.c_lo = c_lo;
         fx.c_hi = c_hi;
+        // At the CTA's last segment every MMA has completed and no load is in flight: the
+        // ring (4 x 48 KB) holds up to 3 other partials' halves (3 x 64 KB).  A CTA stages at
+        // most once (its last segment), so fix_full completes phases 0 and 1.
+        SegIter nx = sg;
+        if (EPI == kPlain && TN == BN && c_hi - c_lo <= 3 && !seg_next(p, nx))
+          fx.stage = reinterpret_cast<const float4*>(smem);
       }
       epilogue_tile<EPI, TN>(p, tacc, fx, r_in, row, nt, bias_s, qr);
       tc_fence_before();
