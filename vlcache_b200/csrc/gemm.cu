@@ -276,6 +276,7 @@ struct Fixup {
   const float4* stage;
   uint64_t* bar;  // completes once per staged half
   bool leader;    // issues the bulk copies
+  volatile int* abort_flag;  // raised when a staged half does not arrive in time
 };
 
 // Stage column half h (chunks [4 h, 4 h + 4): 64 KB of each partial, contiguous in the
@@ -297,7 +298,8 @@ __device__ __forceinline__ void stage_parts(const Params& p, const Fixup& fx, in
       ++j;
     }
   }
-  mbar_wait_bounded(fx.bar, (uint32_t)h, VLC_DEV_ERR_TIMEOUT + 51, VLC_WAIT_LIMIT_CYCLES);
+  // a timeout records the error; the CTA then unwinds after this tile (its values are void)
+  if (!mbar_wait_bounded(fx.bar, (uint32_t)h, VLC_DEV_ERR_TIMEOUT + 51, VLC_WAIT_LIMIT_CYCLES)) *fx.abort_flag = 1;
 }
 
 template <int TN>
@@ -347,7 +349,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tacc, co
     const int n0 = nt * TN;
 #pragma unroll 1
     for (int c = 0; c < TN / 32; ++c) {
-      if (fx.stage != nullptr && c % 4 == 0) stage_parts(p, fx, c / 4);
+      if (fx.stage != nullptr && fx.c_lo <= fx.c_hi && c % 4 == 0) stage_parts(p, fx, c / 4);
       float v[32];
       load_acc32<TN>(p, tacc + c * 32, fx, r_in, c * 32, v);
       const int col = n0 + c * 32;
@@ -626,6 +628,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_kernel(const __grid_const
       fx.stage = nullptr;
       fx.bar = fix_full;
       fx.leader = leader;
+      fx.abort_flag = abort_flag;
       if (EPI != kQkvRope && (sg.kb_lo != 0 || sg.kb_hi != p.k_blocks)) {
         // Stream-K: this CTA covers part of the tile.  Leave the partial, take a ticket.
         // Partial layout: 16-byte piece q (columns 4q .. 4q + 3) of row r at float4 index
@@ -820,10 +823,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) gemm_pair_kernel(const __grid_
     const int quarter = warp & 3;
     const int r_in = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    Fixup fx;
+    Fixup fx;  // whole tiles only: no partials to add, nothing to stage
     fx.t = 0;
     fx.c_lo = 1;
     fx.c_hi = 0;
+    fx.stage = nullptr;
+    fx.bar = nullptr;
+    fx.leader = false;
+    fx.abort_flag = abort_flag;
     __nv_bfloat16* bias_s =
         p.bias != nullptr ? reinterpret_cast<__nv_bfloat16*>(smem + P_OFF_BIAS) + (warp - 2) * 256 : nullptr;
     QkvRow qr;
