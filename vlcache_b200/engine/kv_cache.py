@@ -298,9 +298,11 @@ class WarmPrefillBuilder:
         vidx = 0
         logit_indices: list[int] = []
         any_partial = False
+        total = 0  # table entries so far (running offsets: O(requests))
         for r in reqs:
-            offsets.append(sum(lengths))
+            offsets.append(total)
             lengths.append(len(r.block_table))
+            total += lengths[-1]
             tables.append(np.asarray(r.block_table, dtype=np.int32))
         for i, r in enumerate(reqs):
             n, L, off = r.seqlen, lengths[i], offsets[i]
@@ -333,8 +335,9 @@ class WarmPrefillBuilder:
         for it in reuse:
             r = reqs[it.request]
             count = r.img_end - r.img_start - r.num_recompute
-            old_off = sum(lengths) + sum(len(t) for t in tables[len(reqs):])
+            old_off = total  # after the requests' tables and the earlier old tables
             tables.append(np.asarray(it.old_block_table, dtype=np.int32))
+            total += len(it.old_block_table)
             rdesc.append([out, count, r.img_start + r.num_recompute, offsets[it.request], lengths[it.request],
                           it.old_img_start + r.num_recompute, old_off, len(it.old_block_table)])
             out += count
