@@ -303,7 +303,7 @@ class WarmPrefillBuilder:
             offsets.append(total)
             lengths.append(len(r.block_table))
             total += lengths[-1]
-            tables.append(np.asarray(r.block_table, dtype=np.int32))
+            tables.extend(r.block_table)  # one flat list, converted once below
         for i, r in enumerate(reqs):
             n, L, off = r.seqlen, lengths[i], offsets[i]
             has = L > 0
@@ -336,13 +336,13 @@ class WarmPrefillBuilder:
             r = reqs[it.request]
             count = r.img_end - r.img_start - r.num_recompute
             old_off = total  # after the requests' tables and the earlier old tables
-            tables.append(np.asarray(it.old_block_table, dtype=np.int32))
+            tables.extend(it.old_block_table)
             total += len(it.old_block_table)
             rdesc.append([out, count, r.img_start + r.num_recompute, offsets[it.request], lengths[it.request],
                           it.old_img_start + r.num_recompute, old_off, len(it.old_block_table)])
             out += count
         nv, nr = len(vdesc), len(rdesc)
-        flat_tables = np.concatenate(tables) if tables else np.zeros(0, np.int32)
+        flat_tables = np.asarray(tables, dtype=np.int32)
         desc = np.concatenate([np.asarray(vdesc, np.int32).reshape(-1), np.asarray(rdesc, np.int32).reshape(-1),
                                flat_tables, np.zeros(1, np.int32)])
         desc_dev = torch.from_numpy(desc).pin_memory().to(device, non_blocking=True)
